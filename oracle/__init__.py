@@ -1,0 +1,165 @@
+"""ctypes front-end of the CPU parity oracle (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+cpu_baseline / --impl reference legs of bench.py.  The product package
+(rokoko_b200) never imports this module.
+
+The oracle restates rokoko's inference (src/rokoko.cpp:829-1297 and the kernel
+semantics of src/kernels.cu) in FP32 C++; see oracle/oracle.cpp for the
+function-by-function citations.  Parity status: per-kernel semantics pinned
+against fixtures produced by the reference's own CUDA kernels (tests/golden/);
+the model-level composition is unpinned (the reference ships no golden
+vectors).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int)
+
+
+def build(force: bool = False) -> str:
+    if force or not os.path.exists(_LIB_PATH):
+        subprocess.run(["make", "-C", _HERE, "-s"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.orc_load.restype = ctypes.c_void_p
+        L.orc_load.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+        L.orc_free.argtypes = [ctypes.c_void_p]
+        L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_get_threads.restype = ctypes.c_int
+        L.orc_record_stages.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.orc_get_stage.restype = ctypes.c_long
+        L.orc_get_stage.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _f32p, ctypes.c_long]
+        L.orc_decode_features.restype = ctypes.c_int
+        L.orc_decode_features.argtypes = [ctypes.c_void_p, _f32p, _f32p, _f32p, _f32p, ctypes.c_int, _f32p]
+        L.orc_infer.restype = ctypes.c_int
+        L.orc_infer.argtypes = [ctypes.c_void_p, _i32p, ctypes.c_int, _f32p, _i32p, ctypes.c_int,
+                                _i32p, _i32p, _i32p, _f32p, ctypes.c_long]
+        L.orc_sinegen.argtypes = [_f32p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p]
+        L.orc_stft.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int]
+        L.orc_istft.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int]
+        L.orc_rand_ini.argtypes = [_f32p]
+        _lib = L
+    return _lib
+
+
+def _fp(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def _ip(a: np.ndarray):
+    assert a.dtype == np.int32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_i32p)
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+class Oracle:
+    """One loaded model (KOKO v1 blob).  fp16=True restates the FP16-weights
+    variant (src/rokoko_f16.cpp): FP16 weights and FP16-rounded GEMM inputs."""
+
+    def __init__(self, blob: bytes, fp16: bool = False):
+        err = ctypes.create_string_buffer(256)
+        self._buf = ctypes.create_string_buffer(blob, len(blob))
+        self._h = lib().orc_load(self._buf, len(blob), int(fp16), err, 256)
+        del self._buf
+        if not self._h:
+            raise RuntimeError("oracle load failed: " + err.value.decode())
+        self.fp16 = fp16
+
+    def close(self):
+        if self._h:
+            lib().orc_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def record(self, on: bool = True):
+        lib().orc_record_stages(self._h, int(on))
+
+    def stage(self, name: str) -> np.ndarray | None:
+        n = lib().orc_get_stage(self._h, name.encode(), None, 0)
+        if n == 0:
+            return None
+        out = np.empty(n, np.float32)
+        lib().orc_get_stage(self._h, name.encode(), _fp(out), n)
+        return out
+
+    def decode_features(self, asr, f0, n, style128) -> np.ndarray:
+        asr = np.ascontiguousarray(asr, np.float32)
+        L = asr.shape[0]
+        f0 = np.ascontiguousarray(f0, np.float32)
+        n = np.ascontiguousarray(n, np.float32)
+        s = np.ascontiguousarray(style128, np.float32)
+        out = np.empty(600 * L, np.float32)
+        rc = lib().orc_decode_features(self._h, _fp(asr), _fp(f0), _fp(n), _fp(s), L, _fp(out))
+        if rc:
+            raise RuntimeError("oracle decode failed")
+        return out
+
+    def infer(self, tokens, style256, dur_override=None, bucket: int = 32):
+        tok = np.ascontiguousarray(tokens, np.int32)
+        T = tok.shape[0]
+        s = np.ascontiguousarray(style256, np.float32)
+        dov = None if dur_override is None else np.ascontiguousarray(dur_override, np.int32)
+        dur = np.empty(T, np.int32)
+        L = ctypes.c_int(0)
+        Lb = ctypes.c_int(0)
+        cap = 600 * (int(dov.sum()) if dov is not None else 60 * T) + 1
+        pcm = np.empty(cap, np.float32)
+        rc = lib().orc_infer(self._h, _ip(tok), T, _fp(s), _ip(dov) if dov is not None else None, bucket,
+                             _ip(dur), ctypes.byref(L), ctypes.byref(Lb), _fp(pcm), cap)
+        if rc:
+            raise RuntimeError("oracle infer failed")
+        return pcm[: 600 * L.value].copy(), dur, L.value, Lb.value
+
+
+def sinegen(f0, lw, lb):
+    f0 = np.ascontiguousarray(f0, np.float32)
+    L2 = f0.shape[0]
+    ph = np.empty(L2 * 9, np.float32)
+    src = np.empty(L2 * 300, np.float32)
+    lib().orc_sinegen(_fp(f0), L2, _fp(np.ascontiguousarray(lw, np.float32)),
+                      _fp(np.ascontiguousarray(lb, np.float32)), _fp(ph), _fp(src))
+    return ph.reshape(L2, 9), src
+
+
+def stft(x):
+    x = np.ascontiguousarray(x, np.float32)
+    T2 = x.shape[0] // 5 + 1
+    har = np.empty((T2, 22), np.float32)
+    lib().orc_stft(_fp(x), x.shape[0], _fp(har), T2)
+    return har
+
+
+def istft(c, T_audio):
+    c = np.ascontiguousarray(c, np.float32)
+    y = np.empty(T_audio, np.float32)
+    lib().orc_istft(_fp(c), c.shape[0], _fp(y), T_audio)
+    return y
+
+
+def rand_ini():
+    r = np.empty(9, np.float32)
+    lib().orc_rand_ini(_fp(r))
+    return r

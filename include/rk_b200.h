@@ -1,0 +1,118 @@
+/* rk_b200.h -- C ABI of the B200-native Kokoro decoder / front-half library.
+ *
+ * Plain pointers and sizes only; every function returns an rk_status and
+ * never exits the process.  All model state lives in an opaque rk_ctx (one
+ * per device); separate contexts may be used from separate threads.
+ *
+ * Reference interfaces each entry point replaces (paths in LokalOptima/rokoko):
+ *   rk_conv1d_fprop        cutlass_conv1d_fprop / _f16   src/cutlass_conv.cu:239-313,
+ *                          src/cutlass_conv_f16.cu:216-273 (same argument meaning
+ *                          and return codes 0 / -1 / -2 / -3 / -4)
+ *   rk_create + rk_load_weights_koko
+ *                          Weights::load + precompute_weight_norms
+ *                          src/weights.cpp:500-601, src/rokoko.cpp:1305-1676,
+ *                          src/rokoko_f16.cpp:1177-1197 (KOKO v1 and v2 files)
+ *   rk_infer               rokoko_infer  src/weights.h:402-405,
+ *                          src/rokoko.cpp:829-1297 (tokens + style -> PCM)
+ *   rk_decode_features     the decoder/generator half of rokoko_infer,
+ *                          src/rokoko.cpp:915-1290 (no separate entry exists
+ *                          in the reference; L is used as given, no bucketing)
+ *   rk_compute_decode_bytes  compute_decode_bytes  src/rokoko_common.h:160-229
+ */
+#ifndef RK_B200_H
+#define RK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RK_API __attribute__((visibility("default")))
+#else
+#define RK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int rk_status;
+#define RK_OK 0
+#define RK_ERR_CANNOT_IMPLEMENT (-1) /* unsupported shape / argument */
+#define RK_ERR_WORKSPACE (-2)        /* caller workspace too small */
+#define RK_ERR_INIT (-3)             /* descriptor / context set-up failed */
+#define RK_ERR_LAUNCH (-4)           /* kernel launch failed */
+#define RK_ERR_CUDA (-5)             /* CUDA runtime error (see rk_last_error) */
+#define RK_ERR_WEIGHTS (-6)          /* malformed or incomplete KOKO weight file */
+#define RK_ERR_DEVICE_TIMEOUT (-7)   /* a bounded device-side wait gave up */
+#define RK_ERR_OOM (-8)              /* device allocation failed */
+#define RK_ERR_STATE (-9)            /* call out of order (e.g. no weights loaded) */
+
+#define RK_PRECISION_FP32 0 /* FP32 semantics: 3-pass split-bf16 tensor-core products */
+#define RK_PRECISION_FP16 1 /* FP16-weights semantics (KOKO v2): fp16 x fp16, fp32 accumulate */
+
+typedef struct rk_ctx rk_ctx;
+
+typedef struct rk_options {
+    int precision;  /* RK_PRECISION_* */
+    int max_tokens; /* largest T per utterance (<= 512); 0 = 512 */
+    int l_bucket;   /* decode-length bucket (reference: 32); 0 = 32, 1 = none */
+} rk_options;
+
+RK_API const char* rk_status_string(rk_status s);
+/* Human-readable detail of the last error raised on this thread. */
+RK_API const char* rk_last_error(void);
+
+/* ---- stateless conv seam -------------------------------------------------
+ * y[T_out, C_out] = conv1d(x[T_in, C_in]) with weights w[C_out, K, C_in] (NHWC,
+ * as produced by cutlass_reshape_weights), all FP32 device pointers, time-major.
+ * If residual != NULL: y = conv + residual (bias ignored, as in the reference);
+ * else if bias != NULL: y = conv + bias[C_out]; else y = conv.
+ * precision selects the tensor-core path (RK_PRECISION_*).  stride > 1 requires
+ * dilation == 1.  Enqueued on `stream` (a cudaStream_t, NULL = legacy default).
+ * workspace: device memory of at least rk_conv1d_workspace_size(...) bytes. */
+RK_API size_t rk_conv1d_workspace_size(int C_in, int C_out, int T_in, int K, int stride, int padding, int dilation,
+                                int precision);
+RK_API rk_status rk_conv1d_fprop(const float* x, const float* w, const float* bias, float* y, const float* residual,
+                          void* workspace, size_t workspace_bytes, int C_in, int C_out, int T_in, int K, int stride,
+                          int padding, int dilation, int precision, void* stream);
+/* Synchronises `stream` and reports (and clears) the device error word kept at
+ * the start of a conv workspace: RK_OK or RK_ERR_DEVICE_TIMEOUT. */
+RK_API rk_status rk_conv1d_check(void* workspace, void* stream);
+
+/* ---- model context ------------------------------------------------------- */
+RK_API rk_status rk_create(int device, const rk_options* opts, rk_ctx** out);
+RK_API void rk_destroy(rk_ctx* ctx);
+/* KOKO v1 (fp32) or v2 (pre-baked fp16) bytes in host memory. */
+RK_API rk_status rk_load_weights_koko(rk_ctx* ctx, const void* host_blob, size_t bytes);
+
+/* Decoder + generator on given features, host buffers:
+ * asr [L, 512], f0 [2L], n [2L], style [128] (acoustic half) -> pcm [600 L]. */
+RK_API rk_status rk_decode_features(rk_ctx* ctx, const float* asr, const float* f0, const float* n, const float* style128,
+                             int L, float* pcm_out);
+/* Same on device buffers, enqueued on ctx's stream; pcm is a device pointer. */
+RK_API rk_status rk_decode_features_device(rk_ctx* ctx, const float* d_asr, const float* d_f0, const float* d_n,
+                                    const float* d_style128, int L, float* d_pcm);
+
+/* Full forward for one utterance (rokoko_infer): tokens [T] incl. BOS/EOS,
+ * style [256] (ref_s), optional dur_override [T].  Writes dur_out [T] (may be
+ * NULL), *L_out (frames before bucketing) and min(600 L, pcm_capacity) samples. */
+RK_API rk_status rk_infer(rk_ctx* ctx, const int32_t* tokens, int T, const float* style256, const int32_t* dur_override,
+                   int32_t* dur_out, int* L_out, float* pcm_out, size_t pcm_capacity, size_t* n_samples);
+
+/* Stage activations of the last forward (names as the oracle's stage dumps);
+ * copies min(count, cap) floats; *count = element count (0 if unknown). */
+RK_API rk_status rk_get_stage(rk_ctx* ctx, const char* name, float* host_dst, size_t cap, size_t* count);
+/* Turn per-stage capture on/off (off by default; costs device->host copies). */
+RK_API rk_status rk_record_stages(rk_ctx* ctx, int on);
+
+/* Number of kernels this library launched on ctx since the last reset. */
+RK_API rk_status rk_kernel_count(rk_ctx* ctx, long long* count, int reset);
+/* The CUDA stream (cudaStream_t) all of ctx's work is enqueued on. */
+RK_API void* rk_stream(rk_ctx* ctx);
+
+RK_API size_t rk_compute_decode_bytes(int T, int L);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RK_B200_H */

@@ -1,0 +1,61 @@
+// conv_tc.cuh -- host interface of the tcgen05 implicit-GEMM Conv1d kernel.
+//
+// One kernel covers every dense contraction of the decoder/generator:
+//   Conv1d (any K, dilation; stride 1)      out_row = m,             in_row = m + tap_off[k]
+//   ConvTranspose1d as s polyphase convs   out_row = q*s + r - p,   in_row = q - j   (grid.z = phase r)
+//   Linear / 1x1 conv                       K = 1
+// GEMM view: M = time rows, N = output channels, reduction = taps x input
+// channels.  Activations are [T, Cp] channels-last 16-bit planes (Cp = C_in
+// rounded up to 64, zero padded); weights are [phases*C_out, taps*Cp].
+// FP32 semantics use three bf16 products per step (hi*hi + hi*lo + lo*hi,
+// "split" mode); FP16-weight semantics use one fp16 product.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace rk {
+
+constexpr int CONV_MAX_TAPS = 16;
+
+struct ConvArgs {
+    int M;              // GEMM rows per phase
+    int C_out;          // output channels (the last N tile may be partial)
+    int kblocks;        // Cp / 64
+    int taps;
+    int tap_off[CONV_MAX_TAPS];
+    int a_off;          // in_row = m + a_off + tap_off[k]
+    int b_phase_rows;   // weight-row offset between phases (= C_out), 0 when one phase
+    int T_out;          // valid output rows
+    int o_stride, o_off, o_phase_step;  // out_row = m*o_stride + o_off + phase*o_phase_step
+    float* y;
+    int ldy;
+    const float* bias;  // [C_out] or null
+    const float* res;   // residual rows res[(out_row >> res_shift) * ldres + c] or null
+    int ldres, res_shift;
+    const float* acc_in;  // y = acc_in + v or null
+    int ldacc;
+    float alpha;          // final scale
+    float* stats;         // per-M-tile partial sums [tiles][C_out] then squares [tiles][C_out], or null
+    int stats_parts;      // number of M tiles (offset of the squares block)
+    int dup_row0;         // also write out_row 1 into row 0 (reflection pad (1,0))
+    uint32_t* err;        // device error word
+};
+
+struct ConvOperands {
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;  // a_lo/b_lo unused in fp16 mode
+};
+
+// Encodes a 2-D K-major tile map (box 64 x box_rows, 128B swizzle) over a
+// 16-bit matrix with `rows` rows of `cols` elements and `ld` elements per row.
+bool make_tmap_k64(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, uint64_t rows, uint64_t ld,
+                   uint32_t box_rows);
+
+// Launch; split = three-pass bf16 mode.  n_phases = grid.z.
+cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a, bool split, int n_phases,
+                           cudaStream_t stream);
+
+// N tile the launcher uses for a given C_out (32, 64, 128 or 256).
+int conv_tc_ntile(int C_out);
+
+}  // namespace rk

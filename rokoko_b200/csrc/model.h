@@ -1,0 +1,133 @@
+// model.h -- device-side model state of one rk_ctx: packed weights, the
+// decode workspace and the launch helpers shared by the forward passes.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/rk_b200.h"
+#include "conv_tc.cuh"
+
+namespace rk {
+
+// A conv / linear weight packed for conv_tc: planes [phases*C_out][taps*Cp].
+struct ConvW {
+    int C_in = 0, C_out = 0, K = 0;     // logical shape
+    int taps = 0, Cp = 0, phases = 1;   // packed shape
+    int stride = 1;                     // >1: super-row layout (stride s, dilation 1)
+    void* hi = nullptr;                 // bf16 (split) or fp16
+    void* lo = nullptr;                 // bf16 lo plane (split only)
+    float* bias = nullptr;              // [C_out] or null
+    CUtensorMap tm_hi{}, tm_lo{};
+};
+
+// AdaIN / InstanceNorm parameters: norm weight/bias and the row offset of its
+// style-FC output (gamma = fc[off .. off+C), beta = fc[off+C .. off+2C)).
+struct AdaINW {
+    int C = 0;
+    float* norm_w = nullptr;
+    float* norm_b = nullptr;
+    int fc_off = -1;  // row offset into the style-FC output of its group
+};
+
+struct ResBlk1dW {  // AdainResBlk1d
+    int din = 0, dout = 0;
+    bool shortcut = false, upsample = false;
+    ConvW conv1, conv2, conv1x1;
+    AdaINW norm1, norm2;
+    float* pool_w = nullptr;  // depthwise ConvTranspose1d [din][3]
+    float* pool_b = nullptr;
+};
+
+struct ResBlock1W {  // AdaINResBlock1
+    int C = 0, K = 0;
+    ConvW convs1[3], convs2[3];
+    AdaINW adain1[3], adain2[3];
+    float* alpha1[3] = {nullptr, nullptr, nullptr};
+    float* alpha2[3] = {nullptr, nullptr, nullptr};
+};
+
+struct StyleFC {  // all style FCs driven by one half of the style vector
+    int rows = 0;
+    float* w = nullptr;  // [rows][128]
+    float* b = nullptr;  // [rows]
+    float* out = nullptr;  // [rows]
+};
+
+struct DecoderW {
+    float* f0_conv_w = nullptr;  // [3]
+    float* f0_conv_b = nullptr;
+    float* n_conv_w = nullptr;
+    float* n_conv_b = nullptr;
+    ConvW asr_res;               // 512 -> 64, K=1
+    ResBlk1dW encode, decode[4];
+    ConvW ups[2];                // polyphase ConvTranspose1d
+    ConvW noise_convs[2];        // [0]: super-row stride 6; [1]: K=1
+    ResBlock1W noise_res[2], resblocks[6];
+    ConvW conv_post;
+    float* source_w = nullptr;   // m_source.l_linear [9]
+    float* source_b = nullptr;   // [1]
+    StyleFC fc;                  // acoustic-style FCs (decoder + generator)
+};
+
+struct Buf {  // device allocation tracked for the arena
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+// Operand planes for conv_tc.
+struct Operand {
+    void* hi = nullptr;
+    void* lo = nullptr;
+    size_t plane_bytes = 0;  // capacity of one plane
+};
+
+// Workspace for one decode of up to `cap_L` frames.
+struct DecodeWS {
+    int cap_L = 0;
+    std::vector<void*> allocs;
+    // inputs
+    float *asr = nullptr, *f0 = nullptr, *n = nullptr, *style = nullptr;
+    // decoder
+    float *f0d = nullptr, *nd = nullptr, *cat514 = nullptr, *asr_res = nullptr;
+    float *in1090[4] = {nullptr, nullptr, nullptr, nullptr};
+    float *enc_r1 = nullptr, *enc_sc = nullptr, *dec_out = nullptr;
+    float *stats_cat514 = nullptr, *stats_in[4] = {nullptr, nullptr, nullptr, nullptr};
+    // generator
+    float *phase_low = nullptr, *har_src = nullptr;
+    float *gx = nullptr, *src = nullptr, *u = nullptr, *xa = nullptr, *xb = nullptr, *co = nullptr, *acc = nullptr;
+    float *post = nullptr, *frames = nullptr, *audio = nullptr;
+    float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr, *stats_u = nullptr, *stats_src = nullptr;
+    float* coef = nullptr;  // [2][max C]
+    Operand op_a, op_b, op_har0, op_har1;
+};
+
+struct StageRec {  // captured stage activations (rk_record_stages)
+    std::vector<float> data;
+};
+
+}  // namespace rk
+
+struct rk_ctx {
+    int device = 0;
+    int precision = RK_PRECISION_FP32;
+    int l_bucket = 32;
+    int max_tokens = 512;
+    cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // SineGen / STFT overlap
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    uint32_t* err = nullptr;      // device error word
+    bool loaded = false;
+    std::vector<void*> weight_allocs;
+    rk::DecoderW dec;
+    rk::DecodeWS ws;
+    bool record = false;
+    std::map<std::string, rk::StageRec> stages;
+    long long launches = 0;
+    // decode graphs keyed by L
+    std::unordered_map<int, cudaGraphExec_t> graphs;
+};

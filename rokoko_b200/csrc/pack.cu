@@ -1,0 +1,119 @@
+// pack.cu -- FP32 -> 16-bit operand planes for the tcgen05 conv.
+//
+// The reference casts every activation to FP16 in a separate kernel before
+// each FP16 conv/GEMM (cast_f32_to_f16[_pad], src/kernels.cu:1048-1058,
+// 1283-1302) and applies AdaIN / Snake / LeakyReLU in yet other passes
+// (src/kernels.cu:443-504, 170-183).  Here one pass reads the FP32 tensor and
+// writes the conv's operand directly, channel-padded to a multiple of 64.
+// Split mode writes hi = bf16(v) and lo = bf16(v - hi), so that
+// hi*Whi + hi*Wlo + lo*Whi reproduces an FP32 product to ~2^-16 relative.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "pack.cuh"
+
+namespace rk {
+
+namespace {
+
+__device__ __forceinline__ float act_transform(float v, int c, const PackArgs& a) {
+    if (a.scale) v = a.scale[c] * v + a.shift[c];
+    if (a.snake) {
+        const float al = a.snake[c];
+        const float s = sinf(al * v);
+        v = v + s * s * (1.0f / al);
+    }
+    if (a.lrelu) v = v > 0.0f ? v : a.slope * v;
+    return v;
+}
+
+// one thread = 8 consecutive destination channels of one destination row
+template <bool SPLIT>
+__global__ void pack_act_kernel(PackArgs a) {
+    const int groups = a.Cp >> 3;
+    const long total = (long)a.rows_dst * groups;
+    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int q = (int)(idx / groups);
+        const int g = (int)(idx - (long)q * groups);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int cd = g * 8 + j;          // destination channel
+            const int r = cd / a.C;            // sub-row within the super-row
+            const int c = cd - r * a.C;        // source channel
+            float x = 0.0f;
+            if (r < a.sr_stride) {
+                const int row = q * a.sr_stride - a.sr_pad + r;
+                if (row >= 0 && row < a.rows_src) x = act_transform(a.x[(long)row * a.ldx + c], c, a);
+            }
+            v[j] = x;
+        }
+        if (SPLIT) {
+            __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                h[j] = __float2bfloat16_rn(v[j]);
+                l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+            }
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
+            reinterpret_cast<uint4*>(a.lo)[idx] = *reinterpret_cast<uint4*>(l);
+        } else {
+            __align__(16) __half h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
+template <bool SPLIT>
+__global__ void pack_w_kernel(const float* w, int C_out, int K, int C_in, int stride, int taps, int Cp, void* hi,
+                              void* lo) {
+    const long total = (long)C_out * taps * Cp;
+    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int cd = (int)(idx % Cp);
+        const long t2 = idx / Cp;
+        const int j = (int)(t2 % taps);
+        const int co = (int)(t2 / taps);
+        const int r = cd / C_in, ci = cd - r * C_in;
+        const int k = j * stride + r;
+        float v = 0.0f;
+        if (r < stride && k < K) v = w[((long)co * K + k) * C_in + ci];
+        if (SPLIT) {
+            __nv_bfloat16 h = __float2bfloat16_rn(v);
+            reinterpret_cast<__nv_bfloat16*>(hi)[idx] = h;
+            reinterpret_cast<__nv_bfloat16*>(lo)[idx] = __float2bfloat16_rn(v - __bfloat162float(h));
+        } else {
+            reinterpret_cast<__half*>(hi)[idx] = __float2half_rn(v);
+        }
+    }
+}
+
+int grid_for(long work, int threads) {
+    long b = (work + threads - 1) / threads;
+    if (b > 148L * 16) b = 148L * 16;
+    return (int)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
+    if ((a.Cp & 63) || a.sr_stride < 1) return cudaErrorInvalidValue;
+    const long total = (long)a.rows_dst * (a.Cp >> 3);
+    if (total == 0) return cudaSuccess;
+    if (split) pack_act_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
+    else pack_act_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t pack_weights_nhwc(const float* w, int C_out, int K, int C_in, int stride, void* hi, void* lo,
+                              bool split, cudaStream_t st) {
+    const int taps = (K + stride - 1) / stride;
+    const int Cp = (stride * C_in + 63) / 64 * 64;
+    const long total = (long)C_out * taps * Cp;
+    if (split) pack_w_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(w, C_out, K, C_in, stride, taps, Cp, hi, lo);
+    else pack_w_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(w, C_out, K, C_in, stride, taps, Cp, hi, lo);
+    return cudaGetLastError();
+}
+
+}  // namespace rk

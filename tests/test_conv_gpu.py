@@ -1,0 +1,68 @@
+"""tcgen05 implicit-GEMM conv (rk_conv1d_fprop) vs a float64 torch conv1d.
+
+Tolerances: split-bf16 (FP32 semantics) relative L2 <= 2e-5; fp16 mode
+compares against the float64 conv of the fp16-rounded operands, <= 2e-5.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # C_in, C_out, T_in, K, stride, pad, dil, residual
+    (128, 128, 1000, 3, 1, 1, 1, False),
+    (128, 128, 777, 11, 1, 25, 5, True),
+    (256, 256, 300, 7, 1, 9, 3, False),
+    (514, 1024, 400, 3, 1, 1, 1, False),
+    (1090, 512, 130, 3, 1, 1, 1, True),
+    (22, 256, 4801, 12, 6, 3, 1, False),
+    (128, 22, 901, 7, 1, 3, 1, False),
+    (512, 64, 400, 1, 1, 0, 1, False),
+    (22, 128, 333, 1, 1, 0, 1, False),
+    (768, 2048, 66, 1, 1, 0, 1, False),
+]
+
+
+def _run(rk_lib, C_in, C_out, T_in, K, stride, pad, dil, residual, precision):
+    from rokoko_b200 import lib
+    g = torch.Generator().manual_seed(C_in * 7 + K)
+    x = torch.randn(T_in, C_in, generator=g)
+    w = torch.randn(C_out, C_in, K, generator=g) * (1.0 / np.sqrt(C_in * K))
+    b = torch.randn(C_out, generator=g)
+    T_out = (T_in + 2 * pad - dil * (K - 1) - 1) // stride + 1
+    r = torch.randn(T_out, C_out, generator=g) if residual else None
+    if precision == lib.RK_PRECISION_FP16:
+        xq, wq = x.half().double(), w.half().double()
+    else:
+        xq, wq = x.double(), w.double()
+    ref = torch.nn.functional.conv1d(xq.t()[None], wq, None, stride, pad, dil)[0].t()
+    ref = ref + (r.double() if residual else b.double())
+    dev = torch.device("cuda:0")
+    xd = x.to(dev).contiguous()
+    wd = w.permute(0, 2, 1).contiguous().to(dev)  # NHWC [C_out, K, C_in]
+    bd = b.to(dev)
+    rd = r.to(dev).contiguous() if residual else None
+    yd = torch.full((T_out, C_out), float("nan"), device=dev)
+    ws_bytes = rk_lib.rk_conv1d_workspace_size(C_in, C_out, T_in, K, stride, pad, dil, precision)
+    assert ws_bytes > 0
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=dev)
+    ws_ptr = (ws.data_ptr() + 255) // 256 * 256
+    st = torch.cuda.current_stream().cuda_stream
+    rc = rk_lib.rk_conv1d_fprop(xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), yd.data_ptr(),
+                                rd.data_ptr() if residual else None, ws_ptr, ws_bytes, C_in, C_out, T_in, K,
+                                stride, pad, dil, precision, st)
+    lib.check(rc, "rk_conv1d_fprop")
+    lib.check(rk_lib.rk_conv1d_check(ws_ptr, st), "rk_conv1d_check")
+    y = yd.double().cpu()
+    rel = float((y - ref).norm() / ref.norm())
+    return rel, y, ref
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"ci{c[0]}_co{c[1]}_t{c[2]}_k{c[3]}_s{c[4]}_d{c[6]}" for c in CASES])
+@pytest.mark.parametrize("precision", [0, 1], ids=["split", "fp16"])
+def test_conv_matches_fp64(rk_lib, case, precision):
+    rel, y, ref = _run(rk_lib, *case, precision)
+    assert np.isfinite(y.numpy()).all()
+    assert rel < 2e-5, rel

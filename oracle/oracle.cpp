@@ -19,9 +19,11 @@
 //    (src/kernels.cu:1424); phases themselves follow the reference float
 //    sequence exactly (FMA contraction disabled for this file).
 //  * STFT/iSTFT twiddles and the Hann window are exact values rounded once to
-//    float; the imaginary part of bins 0 and n_fft/2 is exactly +0, so their
-//    phase is 0 or pi (the reference computes sinf(-pi*n) in float and gets a
-//    rounding-noise sign, src/kernels.cu:833-842).
+//    float, and the STFT sums symmetric / antisymmetric pairs, so bins whose
+//    imaginary part is analytically zero (bins 0 and n_fft/2, and every bin of
+//    frame 0, whose reflect-padded input is symmetric) are exactly real with
+//    phase 0 or pi.  The reference evaluates sinf(-2 pi k n / 20) in float and
+//    gets a rounding-noise sign there, i.e. +pi or -pi (src/kernels.cu:833-842).
 //  * InstanceNorm / LayerNorm statistics are accumulated in double (the
 //    reference uses float atomics whose order is nondeterministic,
 //    src/kernels.cu:413-429).
@@ -460,21 +462,28 @@ static void sinegen_source(const float* phase_low, const float* f0, const float*
 }
 
 // ------------------------------------------------------------- STFT / iSTFT
-struct Twiddle { float c[11][20], s[11][20], win[20], win2sum_unused; };
+struct Twiddle { float c[11][20], s[11][20], win[20]; };
+// Periodic Hann window and DFT twiddles cos/sin(2 pi r / 20), evaluated once
+// in double for r <= 10 and mirrored exactly (w[20-n] = w[n], cos(2pi(20-r)/20)
+// = cos, sin = -sin), so symmetric inputs cancel exactly below.
 static const Twiddle& twiddle() {
     static Twiddle tw = [] {
         Twiddle t{};
-        for (int n = 0; n < 20; n++) t.win[n] = (float)(0.5 * (1.0 - std::cos(2.0 * M_PI * n / 20.0)));
+        double cr[20], sr[20], wn[20];
+        for (int r = 0; r <= 10; r++) {
+            cr[r] = std::cos(2.0 * M_PI * r / 20.0);
+            sr[r] = std::sin(2.0 * M_PI * r / 20.0);
+            wn[r] = 0.5 * (1.0 - cr[r]);
+        }
+        cr[0] = 1; sr[0] = 0; cr[5] = 0; sr[5] = 1; cr[10] = -1; sr[10] = 0;
+        wn[0] = 0; wn[10] = 1; wn[5] = 0.5;
+        for (int r = 11; r < 20; r++) { cr[r] = cr[20 - r]; sr[r] = -sr[20 - r]; wn[r] = wn[20 - r]; }
+        for (int n = 0; n < 20; n++) t.win[n] = (float)wn[n];
         for (int k = 0; k < 11; k++)
             for (int n = 0; n < 20; n++) {
-                int r = (k * n) % 20;  // exact angle index: 2*pi*r/20
-                double c = std::cos(2.0 * M_PI * r / 20.0), s = std::sin(2.0 * M_PI * r / 20.0);
-                if (r == 0) { c = 1; s = 0; }
-                if (r == 10) { c = -1; s = 0; }
-                if (r == 5) { c = 0; s = 1; }
-                if (r == 15) { c = 0; s = -1; }
-                t.c[k][n] = (float)c;
-                t.s[k][n] = (float)s;
+                const int r = (k * n) % 20;
+                t.c[k][n] = (float)cr[r];
+                t.s[k][n] = (float)sr[r];
             }
         return t;
     }();
@@ -482,7 +491,13 @@ static const Twiddle& twiddle() {
 }
 
 // STFT (src/kernels.cu:819-879): center reflect pad 10, periodic Hann,
-// X[k] = sum_n x[n] w[n] e^{-2 pi i k n / 20}; mag, atan2 phase.
+// X[k] = sum_n x[n] w[n] e^{-2 pi i k n / 20}; mag, atan2 phase.  Evaluated in
+// symmetric / antisymmetric pairs (n, 20-n):
+//   re = xw0 c0 + xw10 c10 + sum_{n=1..9} (xw[n] + xw[20-n]) c[n]
+//   im = -sum_{n=1..9} (xw[n] - xw[20-n]) s[n]
+// so bins whose imaginary part is analytically zero (k = 0, 10, and every bin
+// of frame 0, whose reflect-padded windowed input is symmetric) come out
+// exactly 0; a zero imaginary part is taken as +0 (phase 0 or pi).
 // Output channels-last har[T2, 22]: [0..11) magnitude, [11..22) phase.
 static void stft(const float* x, int T, float* har, int T2) {
     const Twiddle& tw = twiddle();
@@ -495,13 +510,16 @@ static void stft(const float* x, int T, float* har, int T2) {
                 else if (i >= T) i = 2 * T - 2 - i;
                 xw[n] = x[i] * tw.win[n];
             }
+            float sp[10], dm[10];
+            for (int n = 1; n < 10; n++) { sp[n] = xw[n] + xw[20 - n]; dm[n] = xw[n] - xw[20 - n]; }
             for (int k = 0; k < 11; k++) {
-                float re = 0.f, im = 0.f;
-                for (int n = 0; n < 20; n++) {
-                    re = re + xw[n] * tw.c[k][n];
-                    im = im - xw[n] * tw.s[k][n];
+                float re = xw[0] * tw.c[k][0] + xw[10] * tw.c[k][10];
+                float im = 0.f;
+                for (int n = 1; n < 10; n++) {
+                    re = re + sp[n] * tw.c[k][n];
+                    im = im - dm[n] * tw.s[k][n];
                 }
-                if (k == 0 || k == 10) im = 0.0f;
+                im = im + 0.0f;  // -0 -> +0
                 har[(size_t)f * 22 + k] = sqrtf(re * re + im * im);
                 har[(size_t)f * 22 + 11 + k] = atan2f(im, re);
             }

@@ -1,0 +1,117 @@
+"""Python host front-end over the C ABI (include/rk_b200.h).
+
+`Context` owns one rk_ctx (one CUDA device).  It mirrors the reference's
+model-level entry points: `load_weights` (Weights::load +
+precompute_weight_norms, src/weights.cpp:500-601, src/rokoko.cpp:1305),
+`decode_features` (the decode phase of rokoko_infer, src/rokoko.cpp:915-1290)
+and `infer` (rokoko_infer, src/rokoko.cpp:829-1297).  Every call goes through
+librokoko_b200.so; there is no other implementation behind it.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import lib
+
+FP32 = lib.RK_PRECISION_FP32
+FP16 = lib.RK_PRECISION_FP16
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+def _fp(a):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f32p)
+
+
+def _ip(a):
+    assert a.dtype == np.int32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_i32p)
+
+
+class Context:
+    def __init__(self, device: int = 0, precision: int = FP32, l_bucket: int = 32, max_tokens: int = 512):
+        self._L = lib.load()
+        opts = lib.rk_options(precision, max_tokens, l_bucket)
+        h = ctypes.c_void_p()
+        lib.check(self._L.rk_create(device, ctypes.byref(opts), ctypes.byref(h)), "rk_create")
+        self.h = h
+        self.precision = precision
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.rk_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        return self._L.rk_stream(self.h) or 0
+
+    def load_weights(self, blob: bytes) -> None:
+        buf = (ctypes.c_char * len(blob)).from_buffer_copy(blob) if not isinstance(blob, bytearray) else \
+            (ctypes.c_char * len(blob)).from_buffer(blob)
+        lib.check(self._L.rk_load_weights_koko(self.h, buf, len(blob)), "rk_load_weights_koko")
+
+    def record(self, on: bool = True) -> None:
+        lib.check(self._L.rk_record_stages(self.h, int(on)), "rk_record_stages")
+
+    def stage(self, name: str) -> np.ndarray | None:
+        n = ctypes.c_size_t(0)
+        lib.check(self._L.rk_get_stage(self.h, name.encode(), None, 0, ctypes.byref(n)), "rk_get_stage")
+        if n.value == 0:
+            return None
+        out = np.empty(n.value, np.float32)
+        lib.check(self._L.rk_get_stage(self.h, name.encode(), _fp(out), n.value, ctypes.byref(n)), "rk_get_stage")
+        return out
+
+    def decode_features(self, asr, f0, n, style128) -> np.ndarray:
+        asr = np.ascontiguousarray(asr, np.float32)
+        L = asr.shape[0]
+        f0 = np.ascontiguousarray(f0, np.float32)
+        n = np.ascontiguousarray(n, np.float32)
+        s = np.ascontiguousarray(style128, np.float32)
+        if f0.shape[0] != 2 * L or n.shape[0] != 2 * L or s.shape[0] != 128:
+            raise ValueError("decode_features: f0/n must be [2L], style [128]")
+        pcm = np.empty(600 * L, np.float32)
+        lib.check(self._L.rk_decode_features(self.h, _fp(asr), _fp(f0), _fp(n), _fp(s), L, _fp(pcm)),
+                  "rk_decode_features")
+        return pcm
+
+    def decode_features_device(self, d_asr: int, d_f0: int, d_n: int, d_style: int, L: int, d_pcm: int) -> None:
+        lib.check(self._L.rk_decode_features_device(self.h, d_asr, d_f0, d_n, d_style, L, d_pcm),
+                  "rk_decode_features_device")
+
+    def infer(self, tokens, style256, dur_override=None):
+        tok = np.ascontiguousarray(tokens, np.int32)
+        T = tok.shape[0]
+        s = np.ascontiguousarray(style256, np.float32)
+        dov = None if dur_override is None else np.ascontiguousarray(dur_override, np.int32)
+        dur = np.empty(T, np.int32)
+        L = ctypes.c_int(0)
+        cap = 600 * (int(dov.sum()) if dov is not None else 64 * T)
+        pcm = np.empty(max(cap, 1), np.float32)
+        n = ctypes.c_size_t(0)
+        lib.check(self._L.rk_infer(self.h, _ip(tok), T, _fp(s), _ip(dov) if dov is not None else None, _ip(dur),
+                                   ctypes.byref(L), _fp(pcm), pcm.shape[0], ctypes.byref(n)), "rk_infer")
+        return pcm[: n.value].copy(), dur, L.value
+
+    def kernel_count(self, reset: bool = False) -> int:
+        c = ctypes.c_longlong(0)
+        lib.check(self._L.rk_kernel_count(self.h, ctypes.byref(c), int(reset)), "rk_kernel_count")
+        return c.value

@@ -1,0 +1,223 @@
+// api.cu -- rk_ctx lifecycle and the model-level C-ABI entry points.
+//
+// rk_decode_features* = the decode phase of rokoko_infer (src/rokoko.cpp:915-1290)
+// on caller-given features; rk_infer adds the front half (src/rokoko.cpp:829-914).
+#include <cstring>
+#include <string>
+
+#include "../../include/rk_b200.h"
+#include "decode.h"
+#include "model.h"
+#include "status.h"
+#include "weights.h"
+
+using namespace rk;
+
+namespace {
+
+rk_status check_device_error(rk_ctx* c) {
+    uint32_t e = 0;
+    cudaError_t ce = cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
+    if (ce != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "device sync", ce);
+    if (e) {
+        cudaMemsetAsync(c->err, 0, 4, c->stream);
+        std::string m = "a device-side wait gave up (code " + std::to_string(e) + ")";
+        return fail(RK_ERR_DEVICE_TIMEOUT, m.c_str());
+    }
+    return RK_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" rk_status rk_create(int device, const rk_options* opts, rk_ctx** out) {
+    if (!out) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_create: null out");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return fail(RK_ERR_CUDA, "rk_create: no such CUDA device");
+    }
+    DeviceGuard g(device);
+    rk_ctx* c = new rk_ctx();
+    c->device = device;
+    if (opts) {
+        c->precision = opts->precision;
+        if (opts->max_tokens > 0) c->max_tokens = opts->max_tokens;
+        if (opts->l_bucket > 0) c->l_bucket = opts->l_bucket;
+    }
+    if (c->precision != RK_PRECISION_FP32 && c->precision != RK_PRECISION_FP16) {
+        delete c;
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_create: unknown precision");
+    }
+    if (c->max_tokens > 512) {
+        delete c;
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_create: max_tokens above 512 (ALBERT position table)");
+    }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&c->err, 256) != cudaSuccess || cudaMemset(c->err, 0, 256) != cudaSuccess) {
+        rk_status s = fail_cuda(RK_ERR_CUDA, "rk_create");
+        rk_destroy(c);
+        return s;
+    }
+    *out = c;
+    return RK_OK;
+}
+
+extern "C" void rk_destroy(rk_ctx* c) {
+    if (!c) return;
+    DeviceGuard g(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->side) cudaStreamSynchronize(c->side);
+    free_decode_ws(c);
+    free_weights(c);
+    if (c->err) cudaFree(c->err);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+extern "C" rk_status rk_load_weights_koko(rk_ctx* c, const void* blob, size_t bytes) {
+    if (!c || !blob) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_load_weights_koko: null argument");
+    DeviceGuard g(c->device);
+    return load_weights(c, blob, bytes);
+}
+
+namespace {
+rk_status decode_common(rk_ctx* c, int L) {
+    if (!c->loaded) return fail(RK_ERR_STATE, "no weights loaded");
+    if (L < 1 || L > 64 * 1024) return fail(RK_ERR_CANNOT_IMPLEMENT, "L out of range");
+    return ensure_decode_ws(c, L);
+}
+}  // namespace
+
+extern "C" rk_status rk_decode_features(rk_ctx* c, const float* asr, const float* f0, const float* n,
+                                        const float* style128, int L, float* pcm) {
+    if (!c || !asr || !f0 || !n || !style128 || !pcm) return fail(RK_ERR_CANNOT_IMPLEMENT, "null argument");
+    DeviceGuard g(c->device);
+    rk_status s = decode_common(c, L);
+    if (s) return s;
+    DecodeWS& w = c->ws;
+    cudaStream_t st = c->stream;
+    if (cudaMemcpyAsync(w.asr, asr, (size_t)L * 512 * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.f0, f0, (size_t)2 * L * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.n, n, (size_t)2 * L * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.style, style128, 128 * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "input upload");
+    if (c->record) c->stages.clear();
+    s = enqueue_decode(c, L);
+    if (s) { cudaStreamSynchronize(st); cudaStreamSynchronize(c->side); return s; }
+    if (cudaMemcpyAsync(pcm, w.audio, (size_t)600 * L * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "pcm download");
+    return check_device_error(c);
+}
+
+extern "C" rk_status rk_decode_features_device(rk_ctx* c, const float* d_asr, const float* d_f0, const float* d_n,
+                                               const float* d_style128, int L, float* d_pcm) {
+    if (!c || !d_asr || !d_f0 || !d_n || !d_style128 || !d_pcm)
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "null argument");
+    DeviceGuard g(c->device);
+    rk_status s = decode_common(c, L);
+    if (s) return s;
+    DecodeWS& w = c->ws;
+    cudaStream_t st = c->stream;
+    if (cudaMemcpyAsync(w.asr, d_asr, (size_t)L * 512 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.f0, d_f0, (size_t)2 * L * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.n, d_n, (size_t)2 * L * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.style, d_style128, 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "input copy");
+    s = enqueue_decode(c, L);
+    if (s) return s;
+    if (cudaMemcpyAsync(d_pcm, w.audio, (size_t)600 * L * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "pcm copy");
+    return RK_OK;
+}
+
+extern "C" rk_status rk_record_stages(rk_ctx* c, int on) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    c->record = on != 0;
+    c->stages.clear();
+    return RK_OK;
+}
+
+extern "C" rk_status rk_get_stage(rk_ctx* c, const char* name, float* dst, size_t cap, size_t* count) {
+    if (!c || !name) return fail(RK_ERR_CANNOT_IMPLEMENT, "null argument");
+    auto it = c->stages.find(name);
+    if (count) *count = it == c->stages.end() ? 0 : it->second.data.size();
+    if (it != c->stages.end() && dst)
+        std::memcpy(dst, it->second.data.data(), sizeof(float) * std::min(cap, it->second.data.size()));
+    return RK_OK;
+}
+
+extern "C" rk_status rk_kernel_count(rk_ctx* c, long long* count, int reset) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    if (count) *count = c->launches;
+    if (reset) c->launches = 0;
+    return RK_OK;
+}
+
+extern "C" void* rk_stream(rk_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+// Reference decode-arena size (src/rokoko_common.h:160-229), kept for API
+// compatibility with callers that size their own arenas from it.
+extern "C" size_t rk_compute_decode_bytes(int T, int L) {
+    const size_t L2 = 2 * (size_t)L, TA = L2 * 300, hf = TA / 5 + 1;
+    auto a = [](size_t off, size_t bytes) { return ((off + 255) & ~size_t(255)) + bytes; };
+    size_t off = 0;
+    off = a(off, 128 * 11 * hf * 4);
+    off = a(off, (size_t)T * L * 4);
+    off = a(off, (size_t)L * 640 * 4);
+    off = a(off, (size_t)L * 512 * 4);
+    off = a(off, 512 * L2 * 4);
+    off = a(off, 512 * L2 * 4);
+    off = a(off, 2048 * 4);
+    off = a(off, L2 * 4);
+    off = a(off, L2 * 4);
+    off = a(off, (size_t)L * 512 * 4);
+    off = a(off, (size_t)L * 4);
+    off = a(off, (size_t)L * 4);
+    off = a(off, (size_t)L * 514 * 4);
+    off = a(off, 1090 * L2 * 4);
+    off = a(off, 1090 * L2 * 4);
+    off = a(off, 4 * 1090 * 4);
+    off = a(off, (size_t)L * 1024 * 4);
+    off = a(off, (size_t)L * 64 * 4);
+    off = a(off, L2 * 1090 * 4);
+    for (int i = 0; i < 3; i++) off = a(off, (size_t)L * 1024 * 4);
+    off = a(off, L2 * 512 * 4);
+    off = a(off, 22 * hf * 4);
+    size_t sg = off;
+    sg = a(sg, L2 * 9 * 4);
+    sg = a(sg, TA * 4);
+    sg = a(sg, 9 * 4);
+    off = a(off, hf * 22 * 4);
+    const size_t pool_end = a(off, 5 * 128 * hf * 4);
+    off = sg > pool_end ? sg : pool_end;
+    off = a(off, 512 * 4);
+    off = a(off, TA * 4);
+    return off;
+}
+
+extern "C" rk_status rk_infer(rk_ctx* c, const int32_t*, int, const float*, const int32_t*, int32_t*, int*, float*,
+                              size_t, size_t*) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    return fail(RK_ERR_STATE, "rk_infer: front half not available in this build");
+}

@@ -156,62 +156,55 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const int out_row = m * args.o_stride + args.o_off + phase * args.o_phase_step;
         const bool valid = ok && m < args.M && out_row >= 0 && out_row < args.T_out;
+        const bool dup = valid && out_row == args.dup_src_row;
         const bool want_stats = args.stats != nullptr;
 #pragma unroll 1
         for (int c = 0; c < NB / 32; c++) {
             float v[32];
             tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(c * 32), v);
             const int co0 = n0 + c * 32;
-            const bool full_cols = co0 + 32 <= args.C_out;
+            const int ncol = min(32, args.C_out - co0);
+            float s[32], q[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) { s[j] = 0.f; q[j] = 0.f; }
             if (valid) {
-                if (args.res) {
-                    const float* rp = args.res + (size_t)(out_row >> args.res_shift) * args.ldres + co0;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (full_cols || co0 + j < args.C_out) v[j] += rp[j];
-                }
-                if (args.bias) {
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (full_cols || co0 + j < args.C_out) v[j] += args.bias[co0 + j];
-                }
-                if (args.acc_in) {
-                    const float* ap = args.acc_in + (size_t)out_row * args.ldacc + co0;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (full_cols || co0 + j < args.C_out) v[j] = ap[j] + v[j];
-                }
-                if (args.alpha != 1.0f) {
-#pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] *= args.alpha;
-                }
+                const float* rp = args.res ? args.res + (size_t)(out_row >> args.res_shift) * args.ldres + co0 : nullptr;
+                const float* ap = args.acc_in ? args.acc_in + (size_t)out_row * args.ldacc + co0 : nullptr;
                 float* yp = args.y + (size_t)out_row * args.ldy + co0;
-                if (full_cols && (args.ldy & 3) == 0) {
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(yp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    if (args.dup_row0 && out_row == 1) {
-                        float* y0 = args.y + co0;
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(y0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; j++) {
+                    if (j < ncol) {
+                        float o = v[j];
+                        if (rp) o += rp[j];
+                        if (args.bias) o += args.bias[co0 + j];
+                        if (ap) o = ap[j] + o;
+                        o *= args.alpha;
+                        yp[j] = o;
+                        s[j] = o;
+                        q[j] = o * o;
                     }
-                } else {
-                    for (int j = 0; j < 32; j++)
-                        if (co0 + j < args.C_out) {
-                            yp[j] = v[j];
-                            if (args.dup_row0 && out_row == 1) args.y[co0 + j] = v[j];
+                }
+                if (dup) {
+                    const float* r0 = args.res ? args.res + co0 : nullptr;
+                    const float* a0 = args.acc_in ? args.acc_in + co0 : nullptr;
+                    float* y0 = args.y + co0;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (j < ncol) {
+                            float o = v[j];
+                            if (r0) o += r0[j];
+                            if (args.bias) o += args.bias[co0 + j];
+                            if (a0) o = a0[j] + o;
+                            o *= args.alpha;
+                            y0[j] = o;
+                            s[j] += o;
+                            q[j] += o * o;
                         }
+                    }
                 }
             }
             if (want_stats) {
-                float q[32];
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    v[j] = valid ? v[j] : 0.0f;
-                    q[j] = v[j] * v[j];
-                }
-                const float cs = warp_col_sums(v, lane);
+                const float cs = warp_col_sums(s, lane);
                 const float cq = warp_col_sums(q, lane);
                 red_s[wq][c * 32 + lane] = cs;
                 red_q[wq][c * 32 + lane] = cq;
@@ -219,13 +212,14 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (want_stats) {
             asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int part = blockIdx.z * gridDim.x + blockIdx.x;
             for (int col = threadIdx.x - 64; col < NB; col += 128) {
                 const int co = n0 + col;
                 if (co < args.C_out) {
                     const float s = (red_s[0][col] + red_s[1][col]) + (red_s[2][col] + red_s[3][col]);
                     const float q = (red_q[0][col] + red_q[1][col]) + (red_q[2][col] + red_q[3][col]);
-                    args.stats[(size_t)m_tile * args.C_out + co] = s;
-                    args.stats[(size_t)(args.stats_parts + m_tile) * args.C_out + co] = q;
+                    args.stats[(size_t)part * args.stats_ld + co] = s;
+                    args.stats[(size_t)(args.stats_parts + part) * args.stats_ld + co] = q;
                 }
             }
         }

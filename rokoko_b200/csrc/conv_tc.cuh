@@ -36,9 +36,12 @@ struct ConvArgs {
     const float* acc_in;  // y = acc_in + v or null
     int ldacc;
     float alpha;          // final scale
-    float* stats;         // per-M-tile partial sums [tiles][C_out] then squares [tiles][C_out], or null
-    int stats_parts;      // number of M tiles (offset of the squares block)
-    int dup_row0;         // also write out_row 1 into row 0 (reflection pad (1,0))
+    float* stats;         // per-CTA partial column sums, or null: part p = blockIdx.z*gridDim.x + blockIdx.x
+                          //   sums at stats[p*stats_ld + c], squares at stats[(stats_parts + p)*stats_ld + c]
+    int stats_ld;         // row pitch of the partials (>= C_out; wider for channel-concatenated inputs)
+    int stats_parts;      // gridDim.x * gridDim.z
+    int dup_src_row;      // >= 0: the accumulator of out_row == dup_src_row is also written to row 0
+                          // (with residual row 0): reflection pad (1, 0) of the ConvTranspose output
     uint32_t* err;        // device error word
 };
 

@@ -101,6 +101,7 @@ struct DecodeWS {
     float *phase_low = nullptr, *har_src = nullptr;
     float *gx = nullptr, *src = nullptr, *u = nullptr, *xa = nullptr, *xb = nullptr, *co = nullptr, *acc = nullptr;
     float *post = nullptr, *frames = nullptr, *audio = nullptr;
+    float *har = nullptr, *src2 = nullptr, *gx2 = nullptr;
     float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr, *stats_u = nullptr, *stats_src = nullptr;
     float* coef = nullptr;  // [2][max C]
     Operand op_a, op_b, op_har0, op_har1;

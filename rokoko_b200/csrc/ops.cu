@@ -1,0 +1,392 @@
+// ops.cu -- bandwidth-bound kernels of the decoder / generator.
+//
+// Reference semantics (src/kernels.cu):
+//   AdaIN statistics + affine     :413-504  (here: stats come from the conv
+//                                   epilogue; this file turns them into
+//                                   per-channel scale/shift)
+//   depthwise ConvTranspose1d     :557-594  (fused with AdaIN + LeakyReLU and the
+//                                   operand cast of the next conv)
+//   strided conv F0/N down        :712-746
+//   SineGen phase / source        :1337-1452
+//   STFT / iSTFT                  :819-970  (twiddle tables, gather-form
+//                                   overlap-add without atomics)
+// Float operations that must match the CPU restatement bit-for-bit (SineGen
+// phases, STFT sums) use explicit __fadd_rn / __fmul_rn so the compiler cannot
+// contract them into FMAs.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "ops.cuh"
+
+namespace rk {
+
+namespace {
+
+__constant__ float c_cos[11][20];
+__constant__ float c_sin[11][20];
+__constant__ float c_win[20];
+
+int nblocks(long work, int threads, int cap = 148 * 16) {
+    long b = (work + threads - 1) / threads;
+    if (b > cap) b = cap;
+    return (int)(b < 1 ? 1 : b);
+}
+
+__global__ void style_fc_kernel(const float* __restrict__ W, const float* __restrict__ b,
+                                const float* __restrict__ s, float* __restrict__ out, int rows) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float* w = W + (size_t)warp * 128;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = lane; k < 128; k += 32) acc += w[k] * s[k];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[warp] = acc + b[warp];
+}
+
+__global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, int ld, int col0, int C, int T,
+                                  const float* __restrict__ gamma, const float* __restrict__ beta,
+                                  const float* __restrict__ nw, const float* __restrict__ nb,
+                                  float* __restrict__ coef) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    double s = 0.0, q = 0.0;
+    for (int p = 0; p < parts; p++) {
+        s += stats[(size_t)p * ld + col0 + c];
+        q += stats[(size_t)(parts + p) * ld + col0 + c];
+    }
+    const double mean_d = s / T;
+    const double var_d = q / T - mean_d * mean_d;
+    const float mean = (float)mean_d;
+    const float inv_std = (float)(1.0 / sqrt(var_d + 1e-5));
+    const float g = 1.0f + gamma[c];
+    coef[c] = g * nw[c] * inv_std;
+    coef[C + c] = g * (nb[c] - nw[c] * mean * inv_std) + beta[c];
+}
+
+__global__ void col_stats_kernel(const float* __restrict__ x, int ld, int col0, int ncols, int T,
+                                 int rows_per_part, int parts, float* __restrict__ stats) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int p = blockIdx.y;
+    if (c >= ncols) return;
+    const int r0 = p * rows_per_part, r1 = min(T, r0 + rows_per_part);
+    float s = 0.f, q = 0.f;
+    for (int r = r0; r < r1; r++) {
+        const float v = x[(size_t)r * ld + col0 + c];
+        s += v;
+        q += v * v;
+    }
+    stats[(size_t)p * ld + col0 + c] = s;
+    stats[(size_t)(parts + p) * ld + col0 + c] = q;
+}
+
+__global__ void f0n_down_kernel(const float* __restrict__ f0, const float* __restrict__ n,
+                                const float* __restrict__ wf, const float* __restrict__ bf,
+                                const float* __restrict__ wn, const float* __restrict__ bn, float* f0d, float* nd,
+                                int L) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= L) return;
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < 3; k++) {
+        const int ti = 2 * t - 1 + k;
+        if (ti >= 0 && ti < 2 * L) {
+            a += wf[k] * f0[ti];
+            b += wn[k] * n[ti];
+        }
+    }
+    f0d[t] = a + bf[0];
+    nd[t] = b + bn[0];
+}
+
+__global__ void concat_cols_kernel(float* dst, int ld, int col0, int T, const float* a, int lda, int ca,
+                                   const float* b, int ldb, int cb, const float* c, const float* d) {
+    const int W = ca + cb + (c ? 1 : 0) + (d ? 1 : 0);
+    const long total = (long)T * W;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / W), j = (int)(i - (long)t * W);
+        float v;
+        if (j < ca) v = a[(size_t)t * lda + j];
+        else if (j < ca + cb) v = b[(size_t)t * ldb + (j - ca)];
+        else if (c && j == ca + cb) v = c[t];
+        else v = d[t];
+        dst[(size_t)t * ld + col0 + j] = v;
+    }
+}
+
+template <bool SPLIT>
+__global__ void dw_upsample_pack_kernel(const float* __restrict__ x, int ldx, int T, int C,
+                                        const float* __restrict__ scale, const float* __restrict__ shift,
+                                        float slope, const float* __restrict__ w, const float* __restrict__ bias,
+                                        void* hi, void* lo, int Cp) {
+    const int To = 2 * T;
+    const long total = (long)To * Cp;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / Cp), c = (int)(i - (long)t * Cp);
+        float v = 0.f;
+        if (c < C) {
+            float acc = 0.f;
+            for (int k = 0; k < 3; k++) {
+                const int tu = t + 1 - k;
+                if (tu >= 0 && (tu & 1) == 0 && (tu >> 1) < T) {
+                    float a = scale[c] * x[(size_t)(tu >> 1) * ldx + c] + shift[c];
+                    a = a > 0.f ? a : slope * a;
+                    acc += w[c * 3 + k] * a;
+                }
+            }
+            v = acc + bias[c];
+        }
+        if (SPLIT) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            static_cast<__nv_bfloat16*>(hi)[i] = h;
+            static_cast<__nv_bfloat16*>(lo)[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+        } else {
+            static_cast<__half*>(hi)[i] = __float2half_rn(v);
+        }
+    }
+}
+
+// One thread per harmonic; the cumulative sum runs serially in the same float
+// order as the reference (src/kernels.cu:1352-1383).
+__global__ void sinegen_phase_kernel(const float* __restrict__ f0, int L2, const float* __restrict__ rand_ini,
+                                     float* __restrict__ phase_low) {
+    const int h = threadIdx.x;
+    if (h >= 9) return;
+    const int T_audio = L2 * 300;
+    const float ri = rand_ini[h];
+    float run = 0.f;
+    const float scale = __fmul_rn(__fmul_rn(2.0f, 3.14159265358979323846f), 300.0f);
+    for (int t = 0; t < L2; t++) {
+        float src = __fsub_rn(__fdiv_rn(__fmul_rn(__fadd_rn((float)t, 0.5f), (float)T_audio), (float)L2), 0.5f);
+        src = fmaxf(0.0f, fminf(src, (float)(T_audio - 1)));
+        const int lo = (int)src;
+        const int hi = min(lo + 1, T_audio - 1);
+        const float frac = __fsub_rn(src, (float)lo);
+        float rad_lo = fmodf(__fdiv_rn(__fmul_rn(f0[lo / 300], (float)(h + 1)), 24000.0f), 1.0f);
+        float rad_hi = fmodf(__fdiv_rn(__fmul_rn(f0[hi / 300], (float)(h + 1)), 24000.0f), 1.0f);
+        if (rad_lo < 0.0f) rad_lo = __fadd_rn(rad_lo, 1.0f);
+        if (rad_hi < 0.0f) rad_hi = __fadd_rn(rad_hi, 1.0f);
+        if (lo == 0) rad_lo = __fadd_rn(rad_lo, ri);
+        if (hi == 0) rad_hi = __fadd_rn(rad_hi, ri);
+        const float v = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, frac), rad_lo), __fmul_rn(frac, rad_hi));
+        run = t == 0 ? v : __fadd_rn(run, v);
+        phase_low[t * 9 + h] = __fmul_rn(run, scale);
+    }
+}
+
+__global__ void sinegen_source_kernel(const float* __restrict__ phase_low, const float* __restrict__ f0,
+                                      const float* __restrict__ lw, const float* __restrict__ lb,
+                                      float* __restrict__ out, int L2, int T_audio) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T_audio) return;
+    float src = __fsub_rn(__fdiv_rn(__fmul_rn(__fadd_rn((float)t, 0.5f), (float)L2), (float)T_audio), 0.5f);
+    src = fmaxf(0.0f, fminf(src, (float)(L2 - 1)));
+    const int lo = (int)src;
+    const int hi = min(lo + 1, L2 - 1);
+    const float frac = __fsub_rn(src, (float)lo);
+    const float f0v = f0[t / 300];
+    const float uv = (f0v > 10.0f) ? 1.0f : 0.0f;
+    const float namp = __fadd_rn(__fmul_rn(uv, 0.003f), __fmul_rn(__fsub_rn(1.0f, uv), 0.1f / 3.0f));
+    float sum = lb[0];
+    for (int h = 0; h < 9; h++) {
+        const float ph = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, frac), phase_low[lo * 9 + h]),
+                                   __fmul_rn(frac, phase_low[hi * 9 + h]));
+        const float sine = __fmul_rn(sinf(ph), 0.1f);
+        uint32_t hs = (uint32_t)t * 2654435761u + (uint32_t)h * 340573321u + 42u;
+        hs ^= hs >> 16; hs *= 0x85ebca6bu;
+        hs ^= hs >> 13; hs *= 0xc2b2ae35u; hs ^= hs >> 16;
+        const float u1 = __fdiv_rn((float)((hs & 0xFFFFFFu) + 1u), 16777217.0f);
+        hs = hs * 1664525u + 1013904223u;
+        const float u2 = __fdiv_rn((float)(hs & 0xFFFFFFu), 16777216.0f);
+        const float nz = __fmul_rn(__fmul_rn(sqrtf(__fmul_rn(-2.0f, logf(u1))),
+                                             cosf(__fmul_rn(__fmul_rn(2.0f, 3.14159265358979323846f), u2))),
+                                   namp);
+        const float val = __fadd_rn(__fmul_rn(sine, uv), nz);
+        sum = __fadd_rn(sum, __fmul_rn(val, lw[h]));
+    }
+    out[t] = tanhf(sum);
+}
+
+// One thread per frame.  The DFT is evaluated in symmetric / antisymmetric
+// pairs (n, 20-n) with exactly mirrored window and twiddles:
+//   re = xw0 c0 + xw10 c10 + sum_{n=1..9} (xw[n] + xw[20-n]) c[n]
+//   im = -sum_{n=1..9} (xw[n] - xw[20-n]) s[n]
+// so analytically real bins (k = 0, 10, all bins of the symmetric frame 0)
+// are exactly real; a zero imaginary part is taken as +0.
+__global__ void stft_kernel(const float* __restrict__ x, int T, float* __restrict__ har, int T2) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= T2) return;
+    float xw[20];
+#pragma unroll
+    for (int n = 0; n < 20; n++) {
+        int i = f * 5 + n - 10;
+        if (i < 0) i = -i;
+        else if (i >= T) i = 2 * T - 2 - i;
+        xw[n] = __fmul_rn(x[i], c_win[n]);
+    }
+    float sp[10], dm[10];
+#pragma unroll
+    for (int n = 1; n < 10; n++) { sp[n] = __fadd_rn(xw[n], xw[20 - n]); dm[n] = __fsub_rn(xw[n], xw[20 - n]); }
+#pragma unroll 1
+    for (int k = 0; k < 11; k++) {
+        float re = __fadd_rn(__fmul_rn(xw[0], c_cos[k][0]), __fmul_rn(xw[10], c_cos[k][10]));
+        float im = 0.f;
+#pragma unroll
+        for (int n = 1; n < 10; n++) {
+            re = __fadd_rn(re, __fmul_rn(sp[n], c_cos[k][n]));
+            im = __fsub_rn(im, __fmul_rn(dm[n], c_sin[k][n]));
+        }
+        im = __fadd_rn(im, 0.0f);  // -0 -> +0
+        har[(size_t)f * 22 + k] = sqrtf(__fadd_rn(__fmul_rn(re, re), __fmul_rn(im, im)));
+        har[(size_t)f * 22 + 11 + k] = atan2f(im, re);
+    }
+}
+
+// iSTFT part 1: per frame, spec = exp(c[0:11]), phase = sin(c[11:22]),
+// inverse real DFT (bins 0 and 10 weight 1, others 2) / 20, times the window.
+__global__ void istft_frames_kernel(const float* __restrict__ post, int T2, float* __restrict__ fr) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= T2) return;
+    float re[11], im[11];
+#pragma unroll
+    for (int k = 0; k < 11; k++) {
+        const float mag = expf(post[(size_t)f * 22 + k]);
+        const float ph = sinf(post[(size_t)f * 22 + 11 + k]);
+        re[k] = __fmul_rn(mag, cosf(ph));
+        im[k] = __fmul_rn(mag, sinf(ph));
+    }
+#pragma unroll 4
+    for (int n = 0; n < 20; n++) {
+        float v = 0.f;
+#pragma unroll
+        for (int k = 0; k < 11; k++) {
+            const float contrib = __fsub_rn(__fmul_rn(re[k], c_cos[k][n]), __fmul_rn(im[k], c_sin[k][n]));
+            v = __fadd_rn(v, (k == 0 || k == 10) ? contrib : __fmul_rn(2.0f, contrib));
+        }
+        fr[(size_t)f * 20 + n] = __fmul_rn(__fmul_rn(v, 0.05f), c_win[n]);
+    }
+}
+
+// iSTFT part 2: gather-form overlap-add (each sample sums <= 4 frames in
+// ascending frame order), window-square normalisation, centre pad stripped.
+__global__ void istft_ola_kernel(const float* __restrict__ fr, int T2, float* __restrict__ y, int T_audio) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T_audio) return;
+    const int u = t + 10;
+    float acc = 0.f, ws = 0.f;
+    const int f_hi = min(u / 5, T2 - 1);
+    for (int f = max(0, (u - 15) / 5); f <= f_hi; f++) {
+        const int n = u - 5 * f;
+        if (n < 0 || n >= 20) continue;
+        acc = __fadd_rn(acc, fr[(size_t)f * 20 + n]);
+        ws = __fadd_rn(ws, __fmul_rn(c_win[n], c_win[n]));
+    }
+    y[t] = (ws > 1e-8f) ? __fdiv_rn(acc, ws) : 0.0f;
+}
+
+}  // namespace
+
+void style_fc(const float* W, const float* b, const float* s, float* out, int rows, cudaStream_t st) {
+    style_fc_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(W, b, s, out, rows);
+}
+
+void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
+                const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st) {
+    adain_coef_kernel<<<(C + 127) / 128, 128, 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb, coef);
+}
+
+void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_part, float* stats,
+               cudaStream_t st) {
+    const int parts = (T + rows_per_part - 1) / rows_per_part;
+    dim3 grid((ncols + 127) / 128, parts);
+    col_stats_kernel<<<grid, 128, 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats);
+}
+
+void f0n_down(const float* f0, const float* n, const float* wf, const float* bf, const float* wn, const float* bn,
+              float* f0d, float* nd, int L, cudaStream_t st) {
+    f0n_down_kernel<<<(L + 255) / 256, 256, 0, st>>>(f0, n, wf, bf, wn, bn, f0d, nd, L);
+}
+
+void concat_cols(float* dst, int ld, int col0, int T, const float* a, int lda, int ca, const float* b, int ldb,
+                 int cb, const float* c, const float* d, cudaStream_t st) {
+    const long total = (long)T * (ca + cb + 2);
+    concat_cols_kernel<<<nblocks(total, 256), 256, 0, st>>>(dst, ld, col0, T, a, lda, ca, b, ldb, cb, c, d);
+}
+
+void dw_upsample_pack(const float* x, int ldx, int T, int C, const float* scale, const float* shift, float slope,
+                      const float* w, const float* b, void* hi, void* lo, int Cp, bool split, cudaStream_t st) {
+    const long total = (long)2 * T * Cp;
+    if (split)
+        dw_upsample_pack_kernel<true><<<nblocks(total, 256), 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b,
+                                                                           hi, lo, Cp);
+    else
+        dw_upsample_pack_kernel<false><<<nblocks(total, 256), 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w,
+                                                                            b, hi, lo, Cp);
+}
+
+namespace {
+__device__ float d_rand_ini[9];
+}
+
+void sinegen_phase(const float* f0, int L2, float* phase_low, cudaStream_t st) {
+    float* ri = nullptr;
+    cudaGetSymbolAddress((void**)&ri, d_rand_ini);
+    sinegen_phase_kernel<<<1, 32, 0, st>>>(f0, L2, ri, phase_low);
+}
+
+void sinegen_source(const float* phase_low, const float* f0, const float* lw, const float* lb, float* out, int L2,
+                    cudaStream_t st) {
+    const int T_audio = L2 * 300;
+    sinegen_source_kernel<<<(T_audio + 255) / 256, 256, 0, st>>>(phase_low, f0, lw, lb, out, L2, T_audio);
+}
+
+void stft(const float* x, int T, float* har, int T2, cudaStream_t st) {
+    stft_kernel<<<(T2 + 127) / 128, 128, 0, st>>>(x, T, har, T2);
+}
+
+void istft(const float* post, int T2, float* frames, float* y, int T_audio, cudaStream_t st) {
+    istft_frames_kernel<<<(T2 + 127) / 128, 128, 0, st>>>(post, T2, frames);
+    istft_ola_kernel<<<(T_audio + 255) / 256, 256, 0, st>>>(frames, T2, y, T_audio);
+}
+
+}  // namespace rk
+
+#include <random>
+
+namespace rk {
+// Twiddles, window and SineGen's rand_ini, computed once on the host:
+// angles 2*pi*r/20 evaluated in double for r <= 10, mirrored exactly for
+// r > 10 and rounded to float (quarter angles exact), periodic Hann window
+// mirrored the same way; rand_ini from mt19937(42) +
+// uniform_real_distribution<float>(0, 1) for harmonics 1..8 (src/rokoko.cpp:958-967).
+cudaError_t upload_twiddles() {
+    float cs[11][20], sn[11][20], win[20], ri[9];
+    double cr[20], sr[20], wn[20];
+    for (int r = 0; r <= 10; r++) {
+        cr[r] = std::cos(2.0 * M_PI * r / 20.0);
+        sr[r] = std::sin(2.0 * M_PI * r / 20.0);
+        wn[r] = 0.5 * (1.0 - cr[r]);
+    }
+    cr[0] = 1; sr[0] = 0; cr[5] = 0; sr[5] = 1; cr[10] = -1; sr[10] = 0;
+    wn[0] = 0; wn[10] = 1; wn[5] = 0.5;
+    for (int r = 11; r < 20; r++) { cr[r] = cr[20 - r]; sr[r] = -sr[20 - r]; wn[r] = wn[20 - r]; }
+    for (int n = 0; n < 20; n++) win[n] = (float)wn[n];
+    for (int k = 0; k < 11; k++)
+        for (int n = 0; n < 20; n++) {
+            const int r = (k * n) % 20;
+            cs[k][n] = (float)cr[r];
+            sn[k][n] = (float)sr[r];
+        }
+    std::mt19937 rng(42);
+    std::uniform_real_distribution<float> uni(0.0f, 1.0f);
+    ri[0] = 0.f;
+    for (int h = 1; h < 9; h++) ri[h] = uni(rng);
+    cudaError_t e;
+    if ((e = cudaMemcpyToSymbol(c_cos, cs, sizeof cs)) != cudaSuccess) return e;
+    if ((e = cudaMemcpyToSymbol(c_sin, sn, sizeof sn)) != cudaSuccess) return e;
+    if ((e = cudaMemcpyToSymbol(c_win, win, sizeof win)) != cudaSuccess) return e;
+    return cudaMemcpyToSymbol(d_rand_ini, ri, sizeof ri);
+}
+}  // namespace rk

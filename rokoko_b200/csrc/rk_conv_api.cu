@@ -103,7 +103,7 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
     a.bias = residual ? nullptr : bias;
     a.res = residual; a.ldres = C_out; a.res_shift = 0;
     a.acc_in = nullptr; a.ldacc = 0; a.alpha = 1.0f;
-    a.stats = nullptr; a.stats_parts = 0; a.dup_row0 = 0;
+    a.stats = nullptr; a.stats_ld = 0; a.stats_parts = 0; a.dup_src_row = -1;
     a.err = err;
     if (rk::conv_tc_launch(ops, a, split, 1, st) != cudaSuccess) return rk::fail_cuda(RK_ERR_LAUNCH, "conv_tc");
     return RK_OK;

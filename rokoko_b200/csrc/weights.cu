@@ -1,0 +1,391 @@
+// weights.cu -- KOKO v1/v2 weight files -> packed device weights of one rk_ctx.
+//
+// File format and tensor names: src/weights.cpp:35-50 (parse_header),
+// :57-314 (name -> tensor binding), :320-494 (v2 FP16 companions),
+// :500-564 (header, 4096-aligned data start).  Weight preparation restates
+// precompute_weight_norms (src/rokoko.cpp:1305-1417) and the v1 -> v2
+// converter (scripts/convert_v2.py:87-105): w = g v / ||v|| per output row,
+// FP16 copies for the FP16-weights semantics.
+//
+// Unlike the reference (NHWC [C_out, K, C_in] copies for CUTLASS plus an
+// im2col/col2im path for ConvTranspose1d), every conv here is packed once into
+// the tcgen05 kernel's K-major planes:
+//   Conv1d          [C_out][K][Cp]                   Cp = round_up(C_in, 64)
+//   strided Conv1d  super-rows [C_out][ceil(K/s)][round_up(s*C_in, 64)]
+//   ConvTranspose1d polyphase [s][C_out][K/s][Cp]    (phase r, tap j <- k = r + j*s)
+// FP32 semantics keep two bf16 planes (hi, lo = bf16(w - hi)); FP16 keeps one.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstring>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "model.h"
+#include "ops.cuh"
+#include "status.h"
+#include "weights.h"
+
+namespace rk {
+
+// ------------------------------------------------------------------ parsing
+bool KokoFile::parse(const uint8_t* blob, size_t n, std::string& err) {
+    if (n < 16) { err = "blob too small"; return false; }
+    uint32_t magic;
+    uint64_t hlen;
+    std::memcpy(&magic, blob, 4);
+    std::memcpy(&version, blob + 4, 4);
+    std::memcpy(&hlen, blob + 8, 8);
+    if (magic != 0x4F4B4F4Bu) { err = "bad KOKO magic"; return false; }
+    if (version != 1 && version != 2) { err = "unsupported KOKO version"; return false; }
+    if (16 + hlen > n) { err = "truncated header"; return false; }
+    const size_t data_start = (16 + hlen + 4095) / 4096 * 4096;
+    std::istringstream iss(std::string(reinterpret_cast<const char*>(blob) + 16, hlen));
+    std::string line;
+    while (std::getline(iss, line)) {
+        if (line.empty()) continue;
+        std::istringstream ls(line);
+        KTensor t;
+        std::string name;
+        size_t off;
+        ls >> name >> off >> t.bytes >> t.dtype;
+        int d;
+        while (ls >> d) t.shape.push_back(d);
+        if ((t.dtype != "fp32" && t.dtype != "fp16") || data_start + off + t.bytes > n) {
+            err = "bad tensor entry " + name;
+            return false;
+        }
+        t.data = blob + data_start + off;
+        tensors[name] = t;
+    }
+    return true;
+}
+
+const KTensor* KokoFile::find(const std::string& name) const {
+    auto it = tensors.find(name);
+    return it == tensors.end() ? nullptr : &it->second;
+}
+
+std::vector<float> KokoFile::f32(const std::string& name) const {
+    const KTensor* t = find(name);
+    if (!t) throw WeightError("missing tensor " + name);
+    const size_t n = t->bytes / (t->dtype == "fp32" ? 4 : 2);
+    std::vector<float> v(n);
+    if (t->dtype == "fp32") std::memcpy(v.data(), t->data, n * 4);
+    else {
+        const __half* h = reinterpret_cast<const __half*>(t->data);
+        for (size_t i = 0; i < n; i++) v[i] = __half2float(h[i]);
+    }
+    return v;
+}
+
+// ------------------------------------------------------------------ loader
+namespace {
+
+float f16_round(float x) { return __half2float(__float2half_rn(x)); }
+
+struct Loader {
+    rk_ctx* c;
+    const KokoFile& f;
+    bool split;   // FP32 semantics (bf16 hi/lo planes)
+    bool v2;      // file holds pre-baked FP16 weights
+
+    void* dev_upload(const void* h, size_t bytes) {
+        void* d = nullptr;
+        if (cudaMalloc(&d, bytes) != cudaSuccess) throw WeightError("cudaMalloc failed (weights)");
+        c->weight_allocs.push_back(d);
+        if (cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice) != cudaSuccess) throw WeightError("weight upload failed");
+        return d;
+    }
+    float* dev_f32(const std::vector<float>& v) { return static_cast<float*>(dev_upload(v.data(), v.size() * 4)); }
+    float* dev_tensor(const std::string& name) { return dev_f32(f.f32(name)); }
+
+    // Conv weight as [C_out][C_in][K] floats with weight norm applied (v1) or
+    // from the v2 FP16 companions; FP16 semantics round to half.
+    std::vector<float> conv_weight(const std::string& vname, int Co, int Ci, int K, bool wnorm) {
+        std::vector<float> w((size_t)Co * Ci * K);
+        if (!v2) {
+            std::vector<float> v = f.f32(vname);
+            if (v.size() != w.size()) throw WeightError("shape mismatch " + vname);
+            if (wnorm) {
+                const std::string gname = vname.substr(0, vname.size() - 9) + ".weight_g";
+                std::vector<float> g = f.f32(gname);
+                const size_t fan = (size_t)Ci * K;
+                for (int o = 0; o < Co; o++) {
+                    double ss = 0;
+                    for (size_t i = 0; i < fan; i++) ss += (double)v[o * fan + i] * v[o * fan + i];
+                    const double nrm = std::max(std::sqrt(ss), 1e-12);
+                    for (size_t i = 0; i < fan; i++) w[o * fan + i] = (float)((double)g[o] * v[o * fan + i] / nrm);
+                }
+            } else {
+                w = v;
+            }
+            if (!split)
+                for (auto& x : w) x = f16_round(x);
+            return w;
+        }
+        // v2: NHWC fp16 [Co][K][Ci] (possibly C_in padded) or plain fp16 [Co][Ci][K]
+        if (const KTensor* t = f.find(vname + ".nhwc_f16")) {
+            std::vector<float> n = f.f32(vname + ".nhwc_f16");
+            if (n.size() != w.size()) throw WeightError("shape mismatch " + vname);
+            for (int o = 0; o < Co; o++)
+                for (int k = 0; k < K; k++)
+                    for (int i = 0; i < Ci; i++) w[((size_t)o * Ci + i) * K + k] = n[((size_t)o * K + k) * Ci + i];
+            (void)t;
+            return w;
+        }
+        for (auto& kv : f.tensors) {
+            const std::string pre = vname + ".nhwc_f16_pad";
+            if (kv.first.compare(0, pre.size(), pre) == 0) {
+                const int cp = std::stoi(kv.first.substr(pre.size()));
+                std::vector<float> n = f.f32(kv.first);
+                if (n.size() != (size_t)Co * K * cp) throw WeightError("shape mismatch " + kv.first);
+                for (int o = 0; o < Co; o++)
+                    for (int k = 0; k < K; k++)
+                        for (int i = 0; i < Ci; i++) w[((size_t)o * Ci + i) * K + k] = n[((size_t)o * K + k) * cp + i];
+                return w;
+            }
+        }
+        if (f.find(vname + ".f16")) {
+            std::vector<float> n = f.f32(vname + ".f16");
+            if (n.size() != w.size()) throw WeightError("shape mismatch " + vname);
+            return n;
+        }
+        // FP32 tensors kept in v2 (asr_res, F0/N_conv ...): already weight-normed
+        if (f.find(vname)) return f.f32(vname);
+        throw WeightError("missing tensor " + vname + " (v2)");
+    }
+
+    void make_maps(ConvW& cw) {
+        const int nt = conv_tc_ntile(cw.C_out);
+        const uint64_t cols = (uint64_t)cw.taps * cw.Cp, rows = (uint64_t)cw.phases * cw.C_out;
+        if (!make_tmap_k64(&cw.tm_hi, cw.hi, split, cols, rows, cols, nt) ||
+            (split && !make_tmap_k64(&cw.tm_lo, cw.lo, true, cols, rows, cols, nt)))
+            throw WeightError("tensor map encoding failed (weights)");
+        if (!split) cw.tm_lo = cw.tm_hi;
+    }
+
+    // planes[row][col] <- host floats, converted to bf16 hi/lo or fp16.
+    void upload_planes(ConvW& cw, const std::vector<float>& p) {
+        const size_t n = p.size();
+        if (split) {
+            std::vector<__nv_bfloat16> h(n), l(n);
+            for (size_t i = 0; i < n; i++) {
+                h[i] = __float2bfloat16_rn(p[i]);
+                l[i] = __float2bfloat16_rn(p[i] - __bfloat162float(h[i]));
+            }
+            cw.hi = dev_upload(h.data(), n * 2);
+            cw.lo = dev_upload(l.data(), n * 2);
+        } else {
+            std::vector<__half> h(n);
+            for (size_t i = 0; i < n; i++) h[i] = __float2half_rn(p[i]);
+            cw.hi = dev_upload(h.data(), n * 2);
+            cw.lo = cw.hi;
+        }
+        make_maps(cw);
+    }
+
+    // Conv1d (stride 1) from weight [Co][Ci][K].
+    ConvW conv(const std::string& vname, int Co, int Ci, int K, const char* bias, bool wnorm = true) {
+        ConvW cw;
+        cw.C_in = Ci; cw.C_out = Co; cw.K = K; cw.taps = K; cw.Cp = (Ci + 63) / 64 * 64; cw.phases = 1;
+        std::vector<float> w = conv_weight(vname, Co, Ci, K, wnorm);
+        std::vector<float> p((size_t)Co * K * cw.Cp, 0.f);
+        for (int o = 0; o < Co; o++)
+            for (int i = 0; i < Ci; i++)
+                for (int k = 0; k < K; k++) p[((size_t)o * K + k) * cw.Cp + i] = w[((size_t)o * Ci + i) * K + k];
+        upload_planes(cw, p);
+        if (bias) cw.bias = dev_tensor(bias);
+        return cw;
+    }
+
+    // Strided Conv1d (dilation 1) re-expressed over super-rows of `s` input rows.
+    ConvW conv_strided(const std::string& vname, int Co, int Ci, int K, int s, const char* bias) {
+        ConvW cw;
+        cw.C_in = Ci; cw.C_out = Co; cw.K = K; cw.stride = s;
+        cw.taps = (K + s - 1) / s; cw.Cp = (s * Ci + 63) / 64 * 64; cw.phases = 1;
+        std::vector<float> w = conv_weight(vname, Co, Ci, K, false);
+        std::vector<float> p((size_t)Co * cw.taps * cw.Cp, 0.f);
+        for (int o = 0; o < Co; o++)
+            for (int j = 0; j < cw.taps; j++)
+                for (int r = 0; r < s; r++) {
+                    const int k = j * s + r;
+                    if (k >= K) continue;
+                    for (int i = 0; i < Ci; i++)
+                        p[((size_t)o * cw.taps + j) * cw.Cp + r * Ci + i] = w[((size_t)o * Ci + i) * K + k];
+                }
+        upload_planes(cw, p);
+        if (bias) cw.bias = dev_tensor(bias);
+        return cw;
+    }
+
+    // ConvTranspose1d weight [Ci][Co][K] (weight norm over dim 0 = C_in) as s
+    // polyphase convs with K/s taps: phase r, tap j uses kernel index r + j*s.
+    ConvW conv_transpose(const std::string& vname, int Ci, int Co, int K, int s, const char* bias) {
+        ConvW cw;
+        cw.C_in = Ci; cw.C_out = Co; cw.K = K; cw.phases = s; cw.taps = K / s; cw.Cp = (Ci + 63) / 64 * 64;
+        if (K % s) throw WeightError("ConvTranspose1d kernel not a multiple of the stride");
+        // conv_weight treats dim 0 as the weight-norm row: here dim 0 = C_in, fan = Co*K
+        std::vector<float> w = conv_weight(vname, Ci, Co, K, true);  // [Ci][Co][K]
+        std::vector<float> p((size_t)s * Co * cw.taps * cw.Cp, 0.f);
+        for (int r = 0; r < s; r++)
+            for (int o = 0; o < Co; o++)
+                for (int j = 0; j < cw.taps; j++)
+                    for (int i = 0; i < Ci; i++)
+                        p[(((size_t)r * Co + o) * cw.taps + j) * cw.Cp + i] = w[((size_t)i * Co + o) * K + r + j * s];
+        upload_planes(cw, p);
+        if (bias) cw.bias = dev_tensor(bias);
+        return cw;
+    }
+
+    // ---- style FCs
+    std::vector<float> fcw, fcb;
+    int fc_rows = 0;
+    AdaINW adain(const std::string& pf, int C) {
+        AdaINW a;
+        a.C = C;
+        a.norm_w = dev_tensor(pf + ".norm.weight");
+        a.norm_b = dev_tensor(pf + ".norm.bias");
+        std::vector<float> w = f.f32(v2 ? pf + ".fc.weight.f16" : pf + ".fc.weight");
+        std::vector<float> b = f.f32(pf + ".fc.bias");
+        if (w.size() != (size_t)2 * C * 128 || b.size() != (size_t)2 * C) throw WeightError("bad fc shape " + pf);
+        if (!split && !v2)
+            for (auto& x : w) x = f16_round(x);
+        a.fc_off = fc_rows;
+        fcw.insert(fcw.end(), w.begin(), w.end());
+        fcb.insert(fcb.end(), b.begin(), b.end());
+        fc_rows += 2 * C;
+        return a;
+    }
+    void finish_fc(StyleFC& fc) {
+        fc.rows = fc_rows;
+        fc.w = dev_f32(fcw);
+        fc.b = dev_f32(fcb);
+        float* o = nullptr;
+        if (cudaMalloc(&o, (size_t)fc_rows * 4) != cudaSuccess) throw WeightError("cudaMalloc failed (fc)");
+        c->weight_allocs.push_back(o);
+        fc.out = o;
+        fcw.clear(); fcb.clear(); fc_rows = 0;
+    }
+
+    ResBlk1dW resblk1d(const std::string& pf, int din, int dout, bool shortcut, bool upsample) {
+        ResBlk1dW b;
+        b.din = din; b.dout = dout; b.shortcut = shortcut; b.upsample = upsample;
+        b.norm1 = adain(pf + ".norm1", din);
+        b.norm2 = adain(pf + ".norm2", dout);
+        b.conv1 = conv(pf + ".conv1.weight_v", dout, din, 3, (pf + ".conv1.bias").c_str());
+        b.conv2 = conv(pf + ".conv2.weight_v", dout, dout, 3, (pf + ".conv2.bias").c_str());
+        if (shortcut) b.conv1x1 = conv(pf + ".conv1x1.weight_v", dout, din, 1, nullptr);
+        if (upsample) {
+            // depthwise pool weights stay FP32 (scripts/convert_v2.py:246-248)
+            std::vector<float> w((size_t)din * 3);
+            if (!v2) {
+                std::vector<float> v = f.f32(pf + ".pool.weight_v"), g = f.f32(pf + ".pool.weight_g");
+                for (int o = 0; o < din; o++) {
+                    double ss = 0;
+                    for (int k = 0; k < 3; k++) ss += (double)v[o * 3 + k] * v[o * 3 + k];
+                    const double nrm = std::max(std::sqrt(ss), 1e-12);
+                    for (int k = 0; k < 3; k++) w[o * 3 + k] = (float)((double)g[o] * v[o * 3 + k] / nrm);
+                }
+            } else {
+                w = f.f32(pf + ".pool.weight_v");
+            }
+            b.pool_w = dev_f32(w);
+            b.pool_b = dev_tensor(pf + ".pool.bias");
+        }
+        return b;
+    }
+
+    ResBlock1W resblock1(const std::string& pf, int C, int K) {
+        ResBlock1W r;
+        r.C = C; r.K = K;
+        for (int j = 0; j < 3; j++) {
+            const std::string js = std::to_string(j);
+            r.adain1[j] = adain(pf + ".adain1." + js, C);
+            r.adain2[j] = adain(pf + ".adain2." + js, C);
+            r.convs1[j] = conv(pf + ".convs1." + js + ".weight_v", C, C, K, (pf + ".convs1." + js + ".bias").c_str());
+            r.convs2[j] = conv(pf + ".convs2." + js + ".weight_v", C, C, K, (pf + ".convs2." + js + ".bias").c_str());
+            r.alpha1[j] = dev_tensor(pf + ".alpha1." + js);
+            r.alpha2[j] = dev_tensor(pf + ".alpha2." + js);
+        }
+        return r;
+    }
+
+    // F0_conv / N_conv: Conv1d(1,1,3) with weight norm (FP32 in both files)
+    void small_conv(const std::string& pf, float** w, float** b) {
+        std::vector<float> v = f.f32(pf + ".weight_v");
+        if (!v2) {
+            std::vector<float> g = f.f32(pf + ".weight_g");
+            double ss = 0;
+            for (float x : v) ss += (double)x * x;
+            const double nrm = std::max(std::sqrt(ss), 1e-12);
+            for (auto& x : v) x = (float)((double)g[0] * x / nrm);
+        }
+        *w = dev_f32(v);
+        *b = dev_tensor(pf + ".bias");
+    }
+
+    void load_decoder() {
+        DecoderW& d = c->dec;
+        small_conv("decoder.F0_conv", &d.f0_conv_w, &d.f0_conv_b);
+        small_conv("decoder.N_conv", &d.n_conv_w, &d.n_conv_b);
+        // asr_res stays FP32 in the FP16 variant too (conv1d_f32 with FP32 weights,
+        // src/rokoko_f16.cpp:950-952), so it is always packed as split planes.
+        {
+            const bool keep = split;
+            split = true;
+            d.asr_res = conv("decoder.asr_res.0.weight_v", 64, 512, 1, "decoder.asr_res.0.bias");
+            split = keep;
+        }
+        d.encode = resblk1d("decoder.encode", 514, 1024, true, false);
+        for (int i = 0; i < 4; i++)
+            d.decode[i] = resblk1d("decoder.decode." + std::to_string(i), 1090, i < 3 ? 1024 : 512, true, i == 3);
+        const std::string g = "decoder.generator";
+        d.ups[0] = conv_transpose(g + ".ups.0.weight_v", 512, 256, 20, 10, (g + ".ups.0.bias").c_str());
+        d.ups[1] = conv_transpose(g + ".ups.1.weight_v", 256, 128, 12, 6, (g + ".ups.1.bias").c_str());
+        d.noise_convs[0] = conv_strided(g + ".noise_convs.0.weight", 256, 22, 12, 6, (g + ".noise_convs.0.bias").c_str());
+        d.noise_convs[1] = conv(g + ".noise_convs.1.weight", 128, 22, 1, (g + ".noise_convs.1.bias").c_str(), false);
+        d.noise_res[0] = resblock1(g + ".noise_res.0", 256, 7);
+        d.noise_res[1] = resblock1(g + ".noise_res.1", 128, 11);
+        const int rk_[3] = {3, 7, 11};
+        for (int i = 0; i < 6; i++) d.resblocks[i] = resblock1(g + ".resblocks." + std::to_string(i), i < 3 ? 256 : 128, rk_[i % 3]);
+        d.conv_post = conv(g + ".conv_post.weight_v", 22, 128, 7, (g + ".conv_post.bias").c_str());
+        d.source_w = dev_tensor(g + ".m_source.l_linear.weight");
+        d.source_b = dev_tensor(g + ".m_source.l_linear.bias");
+        finish_fc(d.fc);
+    }
+};
+
+}  // namespace
+
+void free_weights(rk_ctx* c) {
+    for (void* p : c->weight_allocs) cudaFree(p);
+    c->weight_allocs.clear();
+    c->dec = DecoderW{};
+    c->loaded = false;
+}
+
+rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
+    KokoFile f;
+    std::string err;
+    if (!f.parse(static_cast<const uint8_t*>(blob), bytes, err)) return fail(RK_ERR_WEIGHTS, err.c_str());
+    const bool v2 = f.version == 2;
+    if (v2 && c->precision == RK_PRECISION_FP32)
+        return fail(RK_ERR_WEIGHTS, "KOKO v2 holds FP16 weights; create the context with RK_PRECISION_FP16");
+    free_weights(c);
+    try {
+        Loader ld{c, f, c->precision == RK_PRECISION_FP32, v2};
+        ld.load_decoder();
+    } catch (WeightError& e) {
+        free_weights(c);
+        return fail(RK_ERR_WEIGHTS, e.what());
+    }
+    if (upload_twiddles() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "twiddle upload");
+    c->loaded = true;
+    return RK_OK;
+}
+
+}  // namespace rk

@@ -111,6 +111,16 @@ class Context:
                                    ctypes.byref(L), _fp(pcm), pcm.shape[0], ctypes.byref(n)), "rk_infer")
         return pcm[: n.value].copy(), dur, L.value
 
+    def profile(self, on: bool = True) -> None:
+        lib.check(self._L.rk_profile(self.h, int(on)), "rk_profile")
+
+    def profile_read(self):
+        """(conv device ms, conv algorithmic FLOPs, conv launches) since profile(True)."""
+        ms, fl, n = ctypes.c_double(0), ctypes.c_double(0), ctypes.c_longlong(0)
+        lib.check(self._L.rk_profile_read(self.h, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(n)),
+                  "rk_profile_read")
+        return ms.value, fl.value, n.value
+
     def kernel_count(self, reset: bool = False) -> int:
         c = ctypes.c_longlong(0)
         lib.check(self._L.rk_kernel_count(self.h, ctypes.byref(c), int(reset)), "rk_kernel_count")

@@ -67,11 +67,14 @@ extern "C" rk_status rk_create(int device, const rk_options* opts, rk_ctx** out)
         delete c;
         return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_create: max_tokens above 512 (ALBERT position table)");
     }
-    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming) != cudaSuccess ||
-        cudaMalloc(&c->err, 256) != cudaSuccess || cudaMemset(c->err, 0, 256) != cudaSuccess) {
+    bool ok = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&c->rb[0], cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&c->rb[1], cudaStreamNonBlocking) == cudaSuccess;
+    cudaEvent_t* evs[] = {&c->ev_fork, &c->ev_join, &c->ev_src[0], &c->ev_src[1], &c->ev_u, &c->ev_rb[0], &c->ev_rb[1]};
+    for (cudaEvent_t* e : evs) ok = ok && cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaMalloc(&c->err, 256) == cudaSuccess && cudaMemset(c->err, 0, 256) == cudaSuccess;
+    if (!ok) {
         rk_status s = fail_cuda(RK_ERR_CUDA, "rk_create");
         rk_destroy(c);
         return s;
@@ -87,9 +90,13 @@ extern "C" void rk_destroy(rk_ctx* c) {
     if (c->side) cudaStreamSynchronize(c->side);
     free_decode_ws(c);
     free_weights(c);
+    for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     if (c->err) cudaFree(c->err);
-    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
-    if (c->ev_join) cudaEventDestroy(c->ev_join);
+    cudaEvent_t evs[] = {c->ev_fork, c->ev_join, c->ev_src[0], c->ev_src[1], c->ev_u, c->ev_rb[0], c->ev_rb[1]};
+    for (cudaEvent_t e : evs)
+        if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : c->rb)
+        if (s) { cudaStreamSynchronize(s); cudaStreamDestroy(s); }
     if (c->side) cudaStreamDestroy(c->side);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -175,6 +182,37 @@ extern "C" rk_status rk_kernel_count(rk_ctx* c, long long* count, int reset) {
 }
 
 extern "C" void* rk_stream(rk_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+extern "C" rk_status rk_profile(rk_ctx* c, int on) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    c->profile = on != 0;
+    c->prof_used = 0;
+    c->prof_flops.clear();
+    c->prof_ms_acc = 0.0;
+    c->prof_flops_acc = 0.0;
+    c->prof_launches_acc = 0;
+    return RK_OK;
+}
+
+extern "C" rk_status rk_profile_read(rk_ctx* c, double* conv_ms, double* conv_flops, long long* conv_launches) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    DeviceGuard g(c->device);
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "rk_profile_read sync");
+    for (size_t i = 0; i + 1 < c->prof_used; i += 2) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, c->prof_events[i], c->prof_events[i + 1]) != cudaSuccess)
+            return fail_cuda(RK_ERR_CUDA, "rk_profile_read elapsed");
+        c->prof_ms_acc += ms;
+        c->prof_flops_acc += c->prof_flops[i / 2];
+        c->prof_launches_acc++;
+    }
+    c->prof_used = 0;
+    c->prof_flops.clear();
+    if (conv_ms) *conv_ms = c->prof_ms_acc;
+    if (conv_flops) *conv_flops = c->prof_flops_acc;
+    if (conv_launches) *conv_launches = c->prof_launches_acc;
+    return RK_OK;
+}
 
 // Reference decode-arena size (src/rokoko_common.h:160-229), kept for API
 // compatibility with callers that size their own arenas from it.

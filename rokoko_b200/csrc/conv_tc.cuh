@@ -26,7 +26,8 @@ struct ConvArgs {
     int tap_off[CONV_MAX_TAPS];
     int a_off;          // in_row = m + a_off + tap_off[k]
     int b_phase_rows;   // weight-row offset between phases (= C_out), 0 when one phase
-    int T_out;          // valid output rows
+    int T_out;          // valid output rows are [o_min, T_out)
+    int o_min;
     int o_stride, o_off, o_phase_step;  // out_row = m*o_stride + o_off + phase*o_phase_step
     float* y;
     int ldy;
@@ -43,6 +44,10 @@ struct ConvArgs {
     int dup_src_row;      // >= 0: the accumulator of out_row == dup_src_row is also written to row 0
                           // (with residual row 0): reflection pad (1, 0) of the ConvTranspose output
     uint32_t* err;        // device error word
+    // filled by conv_tc_launch
+    int min_off;          // smallest tap offset (the halo tile starts there)
+    int h_pad;            // halo tile rows: 128 + max_off - min_off, rounded up to 8
+    int desc_mode;        // shared-memory descriptor base-offset convention for row-shifted starts
 };
 
 struct ConvOperands {
@@ -54,11 +59,20 @@ struct ConvOperands {
 bool make_tmap_k64(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, uint64_t rows, uint64_t ld,
                    uint32_t box_rows);
 
+// Rows of the activation tile the kernel loads per 64-channel block (the TMA
+// box height of the activation tensor map): 128 + (max - min tap offset),
+// rounded up to a multiple of 8.
+int conv_tc_halo_rows(const int* tap_off, int taps);
+
 // Launch; split = three-pass bf16 mode.  n_phases = grid.z.
 cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a, bool split, int n_phases,
                            cudaStream_t stream);
 
-// N tile the launcher uses for a given C_out (32, 64, 128 or 256).
+// Sets the kernels' dynamic shared-memory limits on the current device (call
+// once per device before the first launch, outside any stream capture).
+cudaError_t conv_tc_init();
+
+// N tile the launcher uses for a given C_out (32, 64 or 128).
 int conv_tc_ntile(int C_out);
 
 }  // namespace rk

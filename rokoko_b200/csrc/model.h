@@ -86,6 +86,15 @@ struct Operand {
     size_t plane_bytes = 0;  // capacity of one plane
 };
 
+// Buffers of one concurrent lane (one stream) of AdaINResBlock1 work.
+struct Lane {
+    cudaStream_t st = nullptr;
+    float *xa = nullptr, *xb = nullptr, *co = nullptr, *out = nullptr;  // [T][C] fp32
+    float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr;   // conv partials
+    float* coef = nullptr;                                               // [2][C]
+    Operand op;
+};
+
 // Workspace for one decode of up to `cap_L` frames.
 struct DecodeWS {
     int cap_L = 0;
@@ -95,16 +104,19 @@ struct DecodeWS {
     // decoder
     float *f0d = nullptr, *nd = nullptr, *cat514 = nullptr, *asr_res = nullptr;
     float *in1090[4] = {nullptr, nullptr, nullptr, nullptr};
-    float *enc_r1 = nullptr, *enc_sc = nullptr, *dec_out = nullptr;
+    float *enc_r1 = nullptr, *enc_sc = nullptr;
     float *stats_cat514 = nullptr, *stats_in[4] = {nullptr, nullptr, nullptr, nullptr};
     // generator
-    float *phase_low = nullptr, *har_src = nullptr;
-    float *gx = nullptr, *src = nullptr, *u = nullptr, *xa = nullptr, *xb = nullptr, *co = nullptr, *acc = nullptr;
+    float *gx = nullptr;                          // decoder output [2L][512]
+    float *phase_low = nullptr, *har_src = nullptr, *har = nullptr;
+    float *src = nullptr, *src2[2] = {nullptr, nullptr}, *stats_src = nullptr;
+    float *u = nullptr, *stats_u = nullptr;
+    float *avg = nullptr;                         // resblock average (only when recording)
     float *post = nullptr, *frames = nullptr, *audio = nullptr;
-    float *har = nullptr, *src2 = nullptr, *gx2 = nullptr;
-    float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr, *stats_u = nullptr, *stats_src = nullptr;
-    float* coef = nullptr;  // [2][max C]
-    Operand op_a, op_b, op_har0, op_har1;
+    Lane lane[3];                                 // resblocks j = 0, 1, 2 (lane 0 also runs the decoder)
+    Lane noise;                                   // noise branch (side stream)
+    Operand op_b;                                 // decoder shortcut operand / ups operand
+    Operand op_har0, op_har1;
 };
 
 struct StageRec {  // captured stage activations (rk_record_stages)
@@ -119,8 +131,13 @@ struct rk_ctx {
     int l_bucket = 32;
     int max_tokens = 512;
     cudaStream_t stream = nullptr;
-    cudaStream_t side = nullptr;  // SineGen / STFT overlap
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaStream_t side = nullptr;  // SineGen / STFT / noise branch
+    cudaStream_t rb[2] = {nullptr, nullptr};  // resblock lanes 1 and 2
+    // fork/join events: fork (main -> side), src[i] (side -> main, noise branch i
+    // done), u (main -> resblock lanes), rb[j] (resblock lane j -> main)
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_src[2] = {nullptr, nullptr}, ev_u = nullptr,
+                ev_rb[2] = {nullptr, nullptr};
+    bool use_graphs = true;
     uint32_t* err = nullptr;      // device error word
     bool loaded = false;
     std::vector<void*> weight_allocs;
@@ -129,6 +146,14 @@ struct rk_ctx {
     bool record = false;
     std::map<std::string, rk::StageRec> stages;
     long long launches = 0;
-    // decode graphs keyed by L
+    // decode graphs keyed by L, and the kernel count each graph replays
     std::unordered_map<int, cudaGraphExec_t> graphs;
+    std::unordered_map<int, long long> graph_launches;
+    // conv profiling (rk_profile): event pairs around each conv launch
+    bool profile = false;
+    std::vector<cudaEvent_t> prof_events;  // pool, 2 per launch
+    size_t prof_used = 0;
+    std::vector<double> prof_flops;        // algorithmic FLOPs of each timed launch
+    double prof_ms_acc = 0.0, prof_flops_acc = 0.0;
+    long long prof_launches_acc = 0;
 };

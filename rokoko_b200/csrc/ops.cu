@@ -47,19 +47,35 @@ __global__ void style_fc_kernel(const float* __restrict__ W, const float* __rest
     if (lane == 0) out[warp] = acc + b[warp];
 }
 
+// block = 32 channels x 32 part-lanes; each lane sums a strided subset of the
+// parts (fixed order), then the 32 lanes are combined in a fixed tree.
 __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, int ld, int col0, int C, int T,
                                   const float* __restrict__ gamma, const float* __restrict__ beta,
                                   const float* __restrict__ nw, const float* __restrict__ nb,
                                   float* __restrict__ coef) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= C) return;
+    __shared__ double sh_s[32][33], sh_q[32][33];
+    const int cx = threadIdx.x, py = threadIdx.y;
+    const int c = blockIdx.x * 32 + cx;
     double s = 0.0, q = 0.0;
-    for (int p = 0; p < parts; p++) {
-        s += stats[(size_t)p * ld + col0 + c];
-        q += stats[(size_t)(parts + p) * ld + col0 + c];
+    if (c < C) {
+        for (int p = py; p < parts; p += 32) {
+            s += stats[(size_t)p * ld + col0 + c];
+            q += stats[(size_t)(parts + p) * ld + col0 + c];
+        }
     }
-    const double mean_d = s / T;
-    const double var_d = q / T - mean_d * mean_d;
+    sh_s[py][cx] = s;
+    sh_q[py][cx] = q;
+    __syncthreads();
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (py < o) {
+            sh_s[py][cx] += sh_s[py + o][cx];
+            sh_q[py][cx] += sh_q[py + o][cx];
+        }
+        __syncthreads();
+    }
+    if (py != 0 || c >= C) return;
+    const double mean_d = sh_s[0][cx] / T;
+    const double var_d = sh_q[0][cx] / T - mean_d * mean_d;
     const float mean = (float)mean_d;
     const float inv_std = (float)(1.0 / sqrt(var_d + 1e-5));
     const float g = 1.0f + gamma[c];
@@ -294,7 +310,8 @@ void style_fc(const float* W, const float* b, const float* s, float* out, int ro
 
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
                 const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st) {
-    adain_coef_kernel<<<(C + 127) / 128, 128, 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb, coef);
+    adain_coef_kernel<<<(C + 31) / 32, dim3(32, 32), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb,
+                                                              coef);
 }
 
 void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_part, float* stats,
@@ -328,12 +345,17 @@ void dw_upsample_pack(const float* x, int ldx, int T, int C, const float* scale,
 
 namespace {
 __device__ float d_rand_ini[9];
+constexpr int kMaxDevices = 64;
+float* g_rand_ini_ptr[kMaxDevices] = {};  // per-device address of d_rand_ini (set by upload_twiddles)
+int cur_dev() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d < kMaxDevices ? d : 0;
+}
 }
 
 void sinegen_phase(const float* f0, int L2, float* phase_low, cudaStream_t st) {
-    float* ri = nullptr;
-    cudaGetSymbolAddress((void**)&ri, d_rand_ini);
-    sinegen_phase_kernel<<<1, 32, 0, st>>>(f0, L2, ri, phase_low);
+    sinegen_phase_kernel<<<1, 32, 0, st>>>(f0, L2, g_rand_ini_ptr[cur_dev()], phase_low);
 }
 
 void sinegen_source(const float* phase_low, const float* f0, const float* lw, const float* lb, float* out, int L2,
@@ -387,6 +409,7 @@ cudaError_t upload_twiddles() {
     if ((e = cudaMemcpyToSymbol(c_cos, cs, sizeof cs)) != cudaSuccess) return e;
     if ((e = cudaMemcpyToSymbol(c_sin, sn, sizeof sn)) != cudaSuccess) return e;
     if ((e = cudaMemcpyToSymbol(c_win, win, sizeof win)) != cudaSuccess) return e;
-    return cudaMemcpyToSymbol(d_rand_ini, ri, sizeof ri);
+    if ((e = cudaMemcpyToSymbol(d_rand_ini, ri, sizeof ri)) != cudaSuccess) return e;
+    return cudaGetSymbolAddress(reinterpret_cast<void**>(&g_rand_ini_ptr[cur_dev()]), d_rand_ini);
 }
 }  // namespace rk

@@ -89,6 +89,47 @@ __global__ void pack_w_kernel(const float* w, int C_out, int K, int C_in, int st
     }
 }
 
+template <bool SPLIT>
+__global__ void pack_avg3_kernel(const float* __restrict__ x0, const float* __restrict__ x1,
+                                 const float* __restrict__ x2, int T, int C, int Cp, float slope, void* hi, void* lo,
+                                 float* f32_out) {
+    const int groups = Cp >> 3;
+    const long total = (long)T * groups;
+    const float third = 1.0f / 3.0f;
+    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(idx / groups);
+        const int g = (int)(idx - (long)t * groups);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = g * 8 + j;
+            float a = 0.f;
+            if (c < C) {
+                const size_t o = (size_t)t * C + c;
+                a = ((x0[o] + x1[o]) + x2[o]) * third;
+                if (f32_out) f32_out[o] = a;
+                a = a > 0.f ? a : slope * a;
+            }
+            v[j] = a;
+        }
+        if (SPLIT) {
+            __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                h[j] = __float2bfloat16_rn(v[j]);
+                l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+            }
+            reinterpret_cast<uint4*>(hi)[idx] = *reinterpret_cast<uint4*>(h);
+            reinterpret_cast<uint4*>(lo)[idx] = *reinterpret_cast<uint4*>(l);
+        } else {
+            __align__(16) __half h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+            reinterpret_cast<uint4*>(hi)[idx] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
 int grid_for(long work, int threads) {
     long b = (work + threads - 1) / threads;
     if (b > 148L * 16) b = 148L * 16;
@@ -103,6 +144,15 @@ cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
     if (total == 0) return cudaSuccess;
     if (split) pack_act_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
     else pack_act_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t pack_avg3(const float* x0, const float* x1, const float* x2, int T, int C, int Cp, float slope, void* hi,
+                      void* lo, bool split, float* f32_out, cudaStream_t st) {
+    if (Cp & 63) return cudaErrorInvalidValue;
+    const long total = (long)T * (Cp >> 3);
+    if (split) pack_avg3_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+    else pack_avg3_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
     return cudaGetLastError();
 }
 

@@ -35,4 +35,12 @@ cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st);
 cudaError_t pack_weights_nhwc(const float* w, int C_out, int K, int C_in, int stride, void* hi, void* lo,
                               bool split, cudaStream_t st);
 
+// Average of the three generator resblocks followed by LeakyReLU, written as
+// the next conv's operand:  v = ((x0 + x1) + x2) * (1/3);  v = lrelu(v, slope).
+// The reference does memset + 3 adds + scale + a separate LeakyReLU
+// (src/rokoko.cpp:1096-1116, 1253).  f32_out (nullable) also receives the
+// average before the LeakyReLU.
+cudaError_t pack_avg3(const float* x0, const float* x1, const float* x2, int T, int C, int Cp, float slope, void* hi,
+                      void* lo, bool split, float* f32_out, cudaStream_t st);
+
 }  // namespace rk

@@ -136,12 +136,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 // layout written by TMA with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), leading offset unused (1), descriptor
 // version 1 (sm_100), layout type 2 = SWIZZLE_128B.
-__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
+// mode 1 additionally sets the base-offset field (bits 49-51) to the start
+// address's row phase within the 1024-byte swizzle pattern.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr, int mode) {
     uint64_t d = 0;
     d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
     d |= (uint64_t)1 << 16;              // LBO (16-byte units), unused for swizzled K-major
     d |= (uint64_t)(1024 >> 4) << 32;    // SBO
     d |= (uint64_t)1 << 46;              // version
+    if (mode == 1) d |= (uint64_t)((smem_addr >> 7) & 7) << 49;
     d |= (uint64_t)2 << 61;              // SWIZZLE_128B
     return d;
 }

@@ -85,11 +85,19 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
     if (rk::pack_weights_nhwc(w, C_out, K, C_in, stride, w_hi, w_lo, split, st) != cudaSuccess)
         return rk::fail_cuda(RK_ERR_LAUNCH, "pack_weights");
 
+    static thread_local int init_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (init_dev != dev) {
+        if (rk::conv_tc_init() != cudaSuccess) return rk::fail_cuda(RK_ERR_INIT, "conv_tc_init");
+        init_dev = dev;
+    }
     rk::ConvOperands ops;
     const int nt = rk::conv_tc_ntile(C_out);
-    if (!rk::make_tmap_k64(&ops.a_hi, a_hi, split, p.Cp, p.rows, p.Cp, 128) ||
+    const int hrows = rk::conv_tc_halo_rows(p.tap_off, p.taps);
+    if (!rk::make_tmap_k64(&ops.a_hi, a_hi, split, p.Cp, p.rows, p.Cp, hrows) ||
         !rk::make_tmap_k64(&ops.b_hi, w_hi, split, (uint64_t)p.taps * p.Cp, C_out, (uint64_t)p.taps * p.Cp, nt) ||
-        (split && (!rk::make_tmap_k64(&ops.a_lo, a_lo, true, p.Cp, p.rows, p.Cp, 128) ||
+        (split && (!rk::make_tmap_k64(&ops.a_lo, a_lo, true, p.Cp, p.rows, p.Cp, hrows) ||
                    !rk::make_tmap_k64(&ops.b_lo, w_lo, true, (uint64_t)p.taps * p.Cp, C_out,
                                       (uint64_t)p.taps * p.Cp, nt))))
         return rk::fail(RK_ERR_INIT, "rk_conv1d_fprop: tensor map encoding failed");
@@ -98,7 +106,7 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
     rk::ConvArgs a{};
     a.M = p.T_out; a.C_out = C_out; a.kblocks = p.Cp / 64; a.taps = p.taps;
     for (int k = 0; k < p.taps; k++) a.tap_off[k] = p.tap_off[k];
-    a.a_off = 0; a.b_phase_rows = 0; a.T_out = p.T_out; a.o_stride = 1; a.o_off = 0; a.o_phase_step = 0;
+    a.a_off = 0; a.b_phase_rows = 0; a.T_out = p.T_out; a.o_min = 0; a.o_stride = 1; a.o_off = 0; a.o_phase_step = 0;
     a.y = y; a.ldy = C_out;
     a.bias = residual ? nullptr : bias;
     a.res = residual; a.ldres = C_out; a.res_shift = 0;

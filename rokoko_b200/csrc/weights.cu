@@ -384,6 +384,7 @@ rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
         return fail(RK_ERR_WEIGHTS, e.what());
     }
     if (upload_twiddles() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "twiddle upload");
+    if (conv_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "conv kernel attributes");
     c->loaded = true;
     return RK_OK;
 }

@@ -56,6 +56,10 @@ SIGNATURES = [
     ("rk_kernel_count", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]),
     ("rk_stream", ctypes.c_void_p, [ctypes.c_void_p]),
     ("rk_compute_decode_bytes", ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ("rk_profile", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    ("rk_profile_read", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+      ctypes.POINTER(ctypes.c_longlong)]),
 ]
 
 

@@ -110,10 +110,11 @@ RK_API rk_status rk_kernel_count(rk_ctx* ctx, long long* count, int reset);
 /* The CUDA stream (cudaStream_t) all of ctx's work is enqueued on. */
 RK_API void* rk_stream(rk_ctx* ctx);
 
-/* Conv profiling: when on, every tcgen05 conv launch is bracketed by CUDA
- * events on its stream.  rk_profile_read synchronises and returns the summed
- * device time (ms), the summed algorithmic FLOPs (2 C_in C_out K T_out; T_in for
- * ConvTranspose1d) and the launch count since rk_profile(ctx, 1). */
+/* Conv profiling: when on, decodes launch eagerly (no CUDA graph) and every
+ * tcgen05 conv launch is bracketed by CUDA events on its stream.
+ * rk_profile_read synchronises and returns the summed device time (ms), the
+ * summed algorithmic FLOPs (2 C_in C_out K T_out; T_in for ConvTranspose1d) and
+ * the launch count since rk_profile(ctx, 1). */
 RK_API rk_status rk_profile(rk_ctx* ctx, int on);
 RK_API rk_status rk_profile_read(rk_ctx* ctx, double* conv_ms, double* conv_flops, long long* conv_launches);
 

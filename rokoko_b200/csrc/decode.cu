@@ -269,9 +269,8 @@ bool ev(cudaError_t e) { return e == cudaSuccess; }
 static size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 void free_decode_ws(rk_ctx* c) {
-    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
     c->graphs.clear();
-    c->graph_launches.clear();
     for (void* p : c->ws.allocs) cudaFree(p);
     c->ws = DecodeWS{};
 }
@@ -476,9 +475,12 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     return r.status;
 }
 
+// One CUDA graph per L.  Stage recording and conv profiling (per-launch
+// timing events) run the same launch sequence eagerly.
 rk_status enqueue_decode(rk_ctx* c, int L) {
     if (c->record || c->profile || !c->use_graphs) return enqueue_decode_body(c, L);
-    auto it = c->graphs.find(L);
+    const std::pair<int, bool> key{L, false};
+    auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
         const long long before = c->launches;
         if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
@@ -488,17 +490,17 @@ rk_status enqueue_decode(rk_ctx* c, int L) {
         cudaError_t e = cudaStreamEndCapture(c->stream, &g);
         if (s != RK_OK) { if (g) cudaGraphDestroy(g); cudaGetLastError(); return s; }
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "graph capture end", e);
-        cudaGraphExec_t ex = nullptr;
-        e = cudaGraphInstantiateWithFlags(&ex, g, 0);
+        rk_ctx::GraphRec rec;
+        e = cudaGraphInstantiateWithFlags(&rec.exec, g, 0);
         cudaGraphDestroy(g);
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "graph instantiate", e);
-        c->graph_launches[L] = c->launches - before;
+        rec.launches = c->launches - before;
         c->launches = before;
-        it = c->graphs.emplace(L, ex).first;
+        it = c->graphs.emplace(key, std::move(rec)).first;
     }
-    cudaError_t e = cudaGraphLaunch(it->second, c->stream);
+    cudaError_t e = cudaGraphLaunch(it->second.exec, c->stream);
     if (e != cudaSuccess) return fail_cuda_err(RK_ERR_LAUNCH, "graph launch", e);
-    c->launches += c->graph_launches[L];
+    c->launches += it->second.launches;
     return RK_OK;
 }
 

@@ -146,9 +146,15 @@ struct rk_ctx {
     bool record = false;
     std::map<std::string, rk::StageRec> stages;
     long long launches = 0;
-    // decode graphs keyed by L, and the kernel count each graph replays
-    std::unordered_map<int, cudaGraphExec_t> graphs;
-    std::unordered_map<int, long long> graph_launches;
+    // decode graphs keyed by (L, profiling): the executable, the kernel count
+    // it replays, and (profiling variant) the conv timing events it records
+    struct GraphRec {
+        cudaGraphExec_t exec = nullptr;
+        long long launches = 0;
+        size_t prof_events = 0;
+        std::vector<double> prof_flops;
+    };
+    std::map<std::pair<int, bool>, GraphRec> graphs;
     // conv profiling (rk_profile): event pairs around each conv launch
     bool profile = false;
     std::vector<cudaEvent_t> prof_events;  // pool, 2 per launch

@@ -125,7 +125,7 @@ class Oracle:
         dur = np.empty(T, np.int32)
         L = ctypes.c_int(0)
         Lb = ctypes.c_int(0)
-        cap = 600 * (int(dov.sum()) if dov is not None else 60 * T) + 1
+        cap = 600 * (int(dov.sum()) if dov is not None else 64 * T) + 1
         pcm = np.empty(cap, np.float32)
         rc = lib().orc_infer(self._h, _ip(tok), T, _fp(s), _ip(dov) if dov is not None else None, bucket,
                              _ip(dur), ctypes.byref(L), ctypes.byref(Lb), _fp(pcm), cap)

@@ -847,10 +847,12 @@ static InferOut infer(Model& m, const int* tok, int T, const float* style, const
         out.dur[t] = std::max(1, (int)std::nearbyint(durf[t]));
     }
     m.dump("dur_float", durf);
+    // out.dur keeps the predicted durations; the alignment uses the override when given
+    std::vector<int> use(out.dur);
     if (dur_override)
-        for (int t = 0; t < T; t++) out.dur[t] = dur_override[t];
+        for (int t = 0; t < T; t++) use[t] = dur_override[t];
     int L = 0;
-    for (int t = 0; t < T; t++) L += out.dur[t];
+    for (int t = 0; t < T; t++) L += use[t];
     out.L = L;
     int Lb = bucket > 1 ? (L + bucket - 1) / bucket * bucket : L;
     out.L_b = Lb;
@@ -860,7 +862,7 @@ static InferOut infer(Model& m, const int* tok, int T, const float* style, const
     {
         int l = 0;
         for (int t = 0; t < T; t++)
-            for (int r = 0; r < out.dur[t]; r++, l++) {
+            for (int r = 0; r < use[t]; r++, l++) {
                 std::memcpy(&en[(size_t)l * 640], &cat[(size_t)t * 640], 640 * 4);
                 std::memcpy(&asr[(size_t)l * 512], &te[(size_t)t * 512], 512 * 4);
             }

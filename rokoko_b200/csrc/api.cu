@@ -2,11 +2,14 @@
 //
 // rk_decode_features* = the decode phase of rokoko_infer (src/rokoko.cpp:915-1290)
 // on caller-given features; rk_infer adds the front half (src/rokoko.cpp:829-914).
+#include <algorithm>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/rk_b200.h"
 #include "decode.h"
+#include "infer.h"
 #include "model.h"
 #include "status.h"
 #include "weights.h"
@@ -89,6 +92,7 @@ extern "C" void rk_destroy(rk_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->side) cudaStreamSynchronize(c->side);
     free_decode_ws(c);
+    free_front_ws(c);
     free_weights(c);
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     if (c->err) cudaFree(c->err);
@@ -254,8 +258,54 @@ extern "C" size_t rk_compute_decode_bytes(int T, int L) {
     return off;
 }
 
-extern "C" rk_status rk_infer(rk_ctx* c, const int32_t*, int, const float*, const int32_t*, int32_t*, int*, float*,
-                              size_t, size_t*) {
-    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
-    return fail(RK_ERR_STATE, "rk_infer: front half not available in this build");
+extern "C" rk_status rk_infer(rk_ctx* c, const int32_t* tokens, int T, const float* style256,
+                              const int32_t* dur_override, int32_t* dur_out, int* L_out, float* pcm,
+                              size_t pcm_capacity, size_t* n_samples) {
+    if (!c || !tokens || !style256) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: null argument");
+    if (!c->loaded) return fail(RK_ERR_STATE, "rk_infer: no weights loaded");
+    if (!c->has_front) return fail(RK_ERR_WEIGHTS, "rk_infer: weight file has no front half (ALBERT / predictor)");
+    if (T < 1 || T > c->max_tokens) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: T out of range");
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= 178) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: token id out of range");
+    if (dur_override)
+        for (int t = 0; t < T; t++)
+            if (dur_override[t] < 0 || dur_override[t] > 4096)
+                return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: duration override out of range");
+    DeviceGuard g(c->device);
+    rk_status s = ensure_front_tokens(c);
+    if (!s) s = ensure_front_frames(c, std::max(512, c->fws.cap_L));
+    if (s) return s;
+    FrontWS& f = c->fws;
+    cudaStream_t st = c->stream;
+    if (c->record) c->stages.clear();
+    if (cudaMemcpyAsync(f.tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(f.style, style256, 256 * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "rk_infer: input upload");
+    s = enqueue_encode(c, T);
+    if (s) { cudaStreamSynchronize(st); return s; }
+    // predicted durations -> host (the one device -> host dependency of the reference, src/rokoko.cpp:790-793)
+    std::vector<int32_t> pred(T), use(T);
+    if (cudaMemcpyAsync(pred.data(), f.dur_i, (size_t)T * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "rk_infer: duration read-back");
+    long long L = 0;
+    for (int t = 0; t < T; t++) { use[t] = dur_override ? dur_override[t] : pred[t]; L += use[t]; }
+    if (dur_out) std::memcpy(dur_out, pred.data(), (size_t)T * 4);
+    if (L < 1 || L > 64 * 1024) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: total duration out of range");
+    const int bucket = c->l_bucket > 1 ? c->l_bucket : 1;
+    const int L_b = (int)((L + bucket - 1) / bucket * bucket);  // src/rokoko.cpp:797-802
+    if (L_out) *L_out = (int)L;
+    s = ensure_decode_ws(c, L_b);
+    if (!s) s = ensure_front_frames(c, L_b);
+    if (s) return s;
+    if (cudaMemcpyAsync(f.dur_use, use.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "rk_infer: duration upload");
+    s = enqueue_predict(c, T, L_b);
+    if (!s) s = enqueue_decode(c, L_b);
+    if (s) { cudaStreamSynchronize(st); return s; }
+    const size_t n = std::min((size_t)600 * (size_t)L, pcm_capacity);
+    if (pcm && n && cudaMemcpyAsync(pcm, c->ws.audio, n * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "rk_infer: pcm download");
+    if (n_samples) *n_samples = pcm ? n : 0;
+    return check_device_error(c);
 }

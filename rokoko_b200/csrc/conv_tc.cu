@@ -48,6 +48,12 @@ struct Cfg {
     static constexpr size_t SMEM_MAX = 1024 + (size_t)NPL * MAX_HPAD * 128 + (size_t)B_STAGES * B_STAGE;
 };
 
+// gelu_new: 0.5 v (1 + tanh(0.7978845608 (v + 0.044715 v^3)))
+__device__ __forceinline__ float gelu_tanh(float v) {
+    const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(inner));
+}
+
 template <int NB, bool SPLIT>
 __global__ void __launch_bounds__(192, 2)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA_hi, const __grid_constant__ CUtensorMap tmA_lo,
@@ -216,6 +222,9 @@ __global__ void __launch_bounds__(192, 2)
                         }
                     }
                     o.x += bias4.x; o.y += bias4.y; o.z += bias4.z; o.w += bias4.w;
+                    if (args.act == 1) {
+                        o.x = gelu_tanh(o.x); o.y = gelu_tanh(o.y); o.z = gelu_tanh(o.z); o.w = gelu_tanh(o.w);
+                    }
                     if (args.acc_in) {
                         const float* ap = args.acc_in + (size_t)orow * args.ldacc + co;
                         o.x = ap[0] + o.x;

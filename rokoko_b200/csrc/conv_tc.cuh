@@ -37,6 +37,7 @@ struct ConvArgs {
     const float* acc_in;  // y = acc_in + v or null
     int ldacc;
     float alpha;          // final scale
+    int act;              // 0: none, 1: tanh-GELU after bias (ALBERT FFN, src/kernels.cu:151-158)
     float* stats;         // per-CTA partial column sums, or null: part p = blockIdx.z*gridDim.x + blockIdx.x
                           //   sums at stats[p*stats_ld + c], squares at stats[(stats_parts + p)*stats_ld + c]
     int stats_ld;         // row pitch of the partials (>= C_out; wider for channel-concatenated inputs)

@@ -20,6 +20,7 @@
 #include <cstring>
 
 #include "decode.h"
+#include "exec.h"
 #include "model.h"
 #include "ops.cuh"
 #include "pack.cuh"
@@ -27,46 +28,7 @@
 
 namespace rk {
 
-namespace {
 
-struct Run {
-    rk_ctx* c;
-    cudaStream_t st;
-    bool split;  // FP32 semantics
-    rk_status status = RK_OK;
-
-    bool ok() const { return status == RK_OK; }
-    void check_launch(const char* what) {
-        c->launches++;
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess && status == RK_OK) status = fail_cuda_err(RK_ERR_LAUNCH, what, e);
-    }
-    void merge(const Run& o) { if (status == RK_OK) status = o.status; }
-};
-
-// conv launch description (defaults: plain stride-1 conv, bias on)
-struct ConvCall {
-    const ConvW* w = nullptr;
-    const Operand* op = nullptr;
-    int rows_in = 0;        // rows of the operand planes
-    bool split = true;
-    int M = 0, T_out = 0;
-    int dil = 1, pad = 0;   // tap_off[k] = k*dil - pad (phases == 1)
-    int a_off = 0;
-    int o_stride = 1, o_off = 0, o_phase_step = 0;
-    float* y = nullptr;
-    int ldy = 0;
-    const float* res = nullptr;
-    int ldres = 0, res_shift = 0;
-    const float* acc_in = nullptr;
-    int ldacc = 0;
-    float alpha = 1.0f;
-    float* stats = nullptr;
-    int stats_ld = 0;
-    int dup_src_row = -1;
-    int o_min = 0;          // first valid output row
-    bool use_bias = true;
-};
 
 int stats_parts_for(const ConvCall& cc) { return ((cc.M + 127) / 128) * cc.w->phases; }
 
@@ -105,6 +67,7 @@ void conv(Run& r, const ConvCall& cc) {
     a.res = cc.res; a.ldres = cc.ldres; a.res_shift = cc.res_shift;
     a.acc_in = cc.acc_in; a.ldacc = cc.ldacc;
     a.alpha = cc.alpha;
+    a.act = cc.act;
     a.stats = cc.stats;
     a.stats_ld = cc.stats_ld ? cc.stats_ld : w.C_out;
     a.stats_parts = stats_parts_for(cc);
@@ -133,8 +96,7 @@ void conv(Run& r, const ConvCall& cc) {
 }
 
 void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, int Cp, bool split,
-          const float* coef = nullptr, const float* snake = nullptr, float slope = 0.f, bool lrelu = false,
-          int sr_stride = 1, int sr_pad = 0, int rows_dst = -1) {
+          const float* coef, const float* snake, float slope, bool lrelu, int sr_stride, int sr_pad, int rows_dst) {
     if (!r.ok()) return;
     PackArgs a{};
     a.x = x; a.ldx = ldx; a.rows_src = rows; a.C = C;
@@ -260,6 +222,8 @@ void resblock1(Run& r, Lane& ln, const ResBlock1W& rb, const float* x0, const fl
         if (j < 2) { x = nxt[j]; sx = nst[j]; px = parts; }
     }
 }
+
+namespace {
 
 bool ev(cudaError_t e) { return e == cudaSuccess; }
 

@@ -74,6 +74,27 @@ struct DecoderW {
     StyleFC fc;                  // acoustic-style FCs (decoder + generator)
 };
 
+struct LstmW {  // one bidirectional LSTM (src/weights.h:242-250)
+    int in = 0;
+    ConvW wih;              // [2048][in]: forward rows 0..1023, reverse 1024..2047; bias = bih + bhh
+    float* whh = nullptr;   // [2][1024][256] recurrent weights (FP16-rounded values in FP16 semantics)
+};
+
+struct FrontW {  // ALBERT, text encoder and prosody predictor
+    float *word = nullptr, *pos = nullptr, *type = nullptr, *emb_ln_w = nullptr, *emb_ln_b = nullptr;
+    ConvW proj, qkv, dense, ffn, ffn_out, bert_enc;
+    float *attn_ln_w = nullptr, *attn_ln_b = nullptr, *ffn_ln_w = nullptr, *ffn_ln_b = nullptr;
+    float* te_embed = nullptr;  // [178][512]
+    ConvW te_conv[3];
+    float *te_ln_g[3] = {}, *te_ln_b[3] = {};
+    LstmW te_lstm, dur_lstm[3], dur_final, shared;
+    int aln_off[3] = {-1, -1, -1};  // AdaLayerNorm fc rows in the prosody style-FC group
+    ConvW dur_proj;
+    ResBlk1dW f0[3], nn[3];
+    float *f0_proj_w = nullptr, *f0_proj_b = nullptr, *n_proj_w = nullptr, *n_proj_b = nullptr;
+    StyleFC fc;  // prosody-style FCs (predictor)
+};
+
 struct Buf {  // device allocation tracked for the arena
     void* p = nullptr;
     size_t bytes = 0;
@@ -119,6 +140,20 @@ struct DecodeWS {
     Operand op_har0, op_har1;
 };
 
+// Front-half workspace: token-sized buffers (allocs) and frame-sized buffers
+// (frame_allocs, grown with the decode length).
+struct FrontWS {
+    std::vector<void*> allocs, frame_allocs;
+    int cap_L = 0;
+    int *tok = nullptr, *dur_i = nullptr, *dur_use = nullptr;
+    float *style = nullptr, *dur_f = nullptr, *emb = nullptr, *h = nullptr, *qkv = nullptr, *ctx = nullptr,
+          *tmp = nullptr, *ffmid = nullptr, *d_en = nullptr, *te = nullptr, *tbuf = nullptr, *cat = nullptr,
+          *lstm_out = nullptr, *proj = nullptr;
+    float *ig = nullptr, *en = nullptr, *shared = nullptr, *x1 = nullptr, *x2 = nullptr, *x3 = nullptr,
+          *stats = nullptr, *stats2 = nullptr;
+    Operand op;
+};
+
 struct StageRec {  // captured stage activations (rk_record_stages)
     std::vector<float> data;
 };
@@ -142,7 +177,10 @@ struct rk_ctx {
     bool loaded = false;
     std::vector<void*> weight_allocs;
     rk::DecoderW dec;
+    rk::FrontW front;
+    bool has_front = false;
     rk::DecodeWS ws;
+    rk::FrontWS fws;
     bool record = false;
     std::map<std::string, rk::StageRec> stages;
     long long launches = 0;

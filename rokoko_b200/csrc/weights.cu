@@ -25,6 +25,7 @@
 #include <vector>
 
 #include "model.h"
+#include "front_ops.cuh"
 #include "ops.cuh"
 #include "status.h"
 #include "weights.h"
@@ -188,18 +189,25 @@ struct Loader {
         make_maps(cw);
     }
 
-    // Conv1d (stride 1) from weight [Co][Ci][K].
-    ConvW conv(const std::string& vname, int Co, int Ci, int K, const char* bias, bool wnorm = true) {
+    // Conv1d (stride 1) from weight [Co][Ci][K] host floats.
+    ConvW conv_host(const std::vector<float>& w, int Co, int Ci, int K, const std::vector<float>* bias) {
         ConvW cw;
         cw.C_in = Ci; cw.C_out = Co; cw.K = K; cw.taps = K; cw.Cp = (Ci + 63) / 64 * 64; cw.phases = 1;
-        std::vector<float> w = conv_weight(vname, Co, Ci, K, wnorm);
         std::vector<float> p((size_t)Co * K * cw.Cp, 0.f);
         for (int o = 0; o < Co; o++)
             for (int i = 0; i < Ci; i++)
                 for (int k = 0; k < K; k++) p[((size_t)o * K + k) * cw.Cp + i] = w[((size_t)o * Ci + i) * K + k];
         upload_planes(cw, p);
-        if (bias) cw.bias = dev_tensor(bias);
+        if (bias) cw.bias = dev_f32(*bias);
         return cw;
+    }
+
+    // Conv1d (stride 1) from weight [Co][Ci][K].
+    ConvW conv(const std::string& vname, int Co, int Ci, int K, const char* bias, bool wnorm = true) {
+        std::vector<float> w = conv_weight(vname, Co, Ci, K, wnorm);
+        std::vector<float> b;
+        if (bias) b = f.f32(bias);
+        return conv_host(w, Co, Ci, K, bias ? &b : nullptr);
     }
 
     // Strided Conv1d (dilation 1) re-expressed over super-rows of `s` input rows.
@@ -357,6 +365,104 @@ struct Loader {
         d.source_b = dev_tensor(g + ".m_source.l_linear.bias");
         finish_fc(d.fc);
     }
+
+    // Linear layer [out][in] (K = 1 conv)
+    ConvW linear(const std::string& wname, int out, int in, const std::string& bname) {
+        return conv(wname, out, in, 1, bname.c_str(), false);
+    }
+
+    LstmW lstm(const std::string& pf, int in) {
+        LstmW l;
+        l.in = in;
+        std::vector<float> wf = conv_weight(pf + ".weight_ih_l0", 1024, in, 1, false);
+        std::vector<float> wr = conv_weight(pf + ".weight_ih_l0_reverse", 1024, in, 1, false);
+        wf.insert(wf.end(), wr.begin(), wr.end());
+        std::vector<float> bias(2048);
+        if (v2) {  // pre-summed bih + bhh (scripts/convert_v2.py:140-146)
+            std::vector<float> bf = f.f32(pf + ".bias_combined_fwd"), br = f.f32(pf + ".bias_combined_rev");
+            std::copy(bf.begin(), bf.end(), bias.begin());
+            std::copy(br.begin(), br.end(), bias.begin() + 1024);
+        } else {  // bias = bih + bhh (src/rokoko.cpp:1392-1398)
+            std::vector<float> a = f.f32(pf + ".bias_ih_l0"), b = f.f32(pf + ".bias_hh_l0");
+            std::vector<float> c = f.f32(pf + ".bias_ih_l0_reverse"), e = f.f32(pf + ".bias_hh_l0_reverse");
+            for (int i = 0; i < 1024; i++) { bias[i] = a[i] + b[i]; bias[1024 + i] = c[i] + e[i]; }
+        }
+        l.wih = conv_host(wf, 2048, in, 1, &bias);
+        std::vector<float> hf = conv_weight(pf + ".weight_hh_l0", 1024, 256, 1, false);
+        std::vector<float> hr = conv_weight(pf + ".weight_hh_l0_reverse", 1024, 256, 1, false);
+        hf.insert(hf.end(), hr.begin(), hr.end());
+        l.whh = dev_f32(hf);
+        return l;
+    }
+
+    int fc_block(const std::string& pf, int rows) {  // plain style FC (AdaLayerNorm): [rows][128] + bias
+        std::vector<float> w = f.f32(v2 ? pf + ".fc.weight.f16" : pf + ".fc.weight");
+        std::vector<float> b = f.f32(pf + ".fc.bias");
+        if (w.size() != (size_t)rows * 128 || b.size() != (size_t)rows) throw WeightError("bad fc shape " + pf);
+        if (!split && !v2)
+            for (auto& x : w) x = f16_round(x);
+        const int off = fc_rows;
+        fcw.insert(fcw.end(), w.begin(), w.end());
+        fcb.insert(fcb.end(), b.begin(), b.end());
+        fc_rows += rows;
+        return off;
+    }
+
+    void load_front() {
+        FrontW& F = c->front;
+        F.word = dev_tensor("bert.embeddings.word_embeddings.weight");
+        F.pos = dev_tensor("bert.embeddings.position_embeddings.weight");
+        F.type = dev_tensor("bert.embeddings.token_type_embeddings.weight");
+        F.emb_ln_w = dev_tensor("bert.embeddings.LayerNorm.weight");
+        F.emb_ln_b = dev_tensor("bert.embeddings.LayerNorm.bias");
+        F.proj = linear("bert.encoder.embedding_hidden_mapping_in.weight", 768, 128,
+                        "bert.encoder.embedding_hidden_mapping_in.bias");
+        const std::string a = "bert.encoder.albert_layer_groups.0.albert_layers.0";
+        {  // fused Q | K | V projection (three TN+bias GEMMs in the reference, src/rokoko.cpp:356-361)
+            std::vector<float> w, b;
+            for (const char* n : {"query", "key", "value"}) {
+                std::vector<float> wi = conv_weight(a + ".attention." + n + ".weight", 768, 768, 1, false);
+                std::vector<float> bi = f.f32(a + ".attention." + n + ".bias");
+                w.insert(w.end(), wi.begin(), wi.end());
+                b.insert(b.end(), bi.begin(), bi.end());
+            }
+            F.qkv = conv_host(w, 2304, 768, 1, &b);
+        }
+        F.dense = linear(a + ".attention.dense.weight", 768, 768, a + ".attention.dense.bias");
+        F.attn_ln_w = dev_tensor(a + ".attention.LayerNorm.weight");
+        F.attn_ln_b = dev_tensor(a + ".attention.LayerNorm.bias");
+        F.ffn = linear(a + ".ffn.weight", 2048, 768, a + ".ffn.bias");
+        F.ffn_out = linear(a + ".ffn_output.weight", 768, 2048, a + ".ffn_output.bias");
+        F.ffn_ln_w = dev_tensor(a + ".full_layer_layer_norm.weight");
+        F.ffn_ln_b = dev_tensor(a + ".full_layer_layer_norm.bias");
+        F.bert_enc = linear("bert_encoder.weight", 512, 768, "bert_encoder.bias");
+        F.te_embed = dev_tensor("text_encoder.embedding.weight");
+        for (int i = 0; i < 3; i++) {
+            const std::string pf = "text_encoder.cnn." + std::to_string(i);
+            F.te_conv[i] = conv(pf + ".0.weight_v", 512, 512, 5, (pf + ".0.bias").c_str());
+            F.te_ln_g[i] = dev_tensor(pf + ".1.gamma");
+            F.te_ln_b[i] = dev_tensor(pf + ".1.beta");
+        }
+        F.te_lstm = lstm("text_encoder.lstm", 512);
+        for (int i = 0; i < 3; i++) {
+            F.dur_lstm[i] = lstm("predictor.text_encoder.lstms." + std::to_string(2 * i), 640);
+            F.aln_off[i] = fc_block("predictor.text_encoder.lstms." + std::to_string(2 * i + 1), 1024);
+        }
+        F.dur_final = lstm("predictor.lstm", 640);
+        F.dur_proj = linear("predictor.duration_proj.linear_layer.weight", 50, 512,
+                            "predictor.duration_proj.linear_layer.bias");
+        F.shared = lstm("predictor.shared", 640);
+        const int din[3] = {512, 512, 256}, dout[3] = {512, 256, 256};
+        for (int i = 0; i < 3; i++) {
+            F.f0[i] = resblk1d("predictor.F0." + std::to_string(i), din[i], dout[i], i == 1, i == 1);
+            F.nn[i] = resblk1d("predictor.N." + std::to_string(i), din[i], dout[i], i == 1, i == 1);
+        }
+        F.f0_proj_w = dev_tensor("predictor.F0_proj.weight");
+        F.f0_proj_b = dev_tensor("predictor.F0_proj.bias");
+        F.n_proj_w = dev_tensor("predictor.N_proj.weight");
+        F.n_proj_b = dev_tensor("predictor.N_proj.bias");
+        finish_fc(F.fc);
+    }
 };
 
 }  // namespace
@@ -365,6 +471,8 @@ void free_weights(rk_ctx* c) {
     for (void* p : c->weight_allocs) cudaFree(p);
     c->weight_allocs.clear();
     c->dec = DecoderW{};
+    c->front = FrontW{};
+    c->has_front = false;
     c->loaded = false;
 }
 
@@ -379,12 +487,16 @@ rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
     try {
         Loader ld{c, f, c->precision == RK_PRECISION_FP32, v2};
         ld.load_decoder();
+        // the front half is optional: decoder-only files (and callers) use rk_decode_features
+        c->has_front = f.find("bert.embeddings.word_embeddings.weight") != nullptr;
+        if (c->has_front) ld.load_front();
     } catch (WeightError& e) {
         free_weights(c);
         return fail(RK_ERR_WEIGHTS, e.what());
     }
     if (upload_twiddles() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "twiddle upload");
     if (conv_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "conv kernel attributes");
+    if (bilstm_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "lstm kernel attributes");
     c->loaded = true;
     return RK_OK;
 }

@@ -1,0 +1,64 @@
+"""Full forward (rk_infer = rokoko_infer) on the B200 vs the CPU FP32 oracle.
+
+Bars: predicted durations bit-exact, L and the sample count (600 L) exact,
+per-stage activations close, waveform relative L2 <= 1e-3 (FP32 semantics).
+Config 0 shapes: 64 phonemes (T = 66), durations overridden by seeded U[2,8]
+(so L ~ 330 -> bucket 352); a smaller T = 20 case runs the predicted
+durations (no override) through the whole pipeline.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+STAGES = [("bert", 1e-4), ("d_en", 1e-4), ("text_enc", 1e-4), ("dur_enc", 1e-4), ("dur_float", 1e-5),
+          ("shared", 2e-4), ("asr_aligned", 1e-4), ("f0_pred", 1e-3), ("n_pred", 1e-3)]
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def oracle_model(v1_blob):
+    import oracle
+    oracle.set_threads(8)
+    m = oracle.Oracle(v1_blob)
+    m.record(True)
+    return m
+
+
+@pytest.fixture(scope="module")
+def gpu_ctx(v1_blob):
+    from rokoko_b200.context import FP32, Context
+    ctx = Context(0, FP32)
+    ctx.load_weights(v1_blob)
+    ctx.record(True)
+    yield ctx
+    ctx.close()
+
+
+@pytest.mark.parametrize("n_phon,override", [(64, True), (18, False)])
+def test_infer_fp32(gpu_ctx, oracle_model, n_phon, override):
+    from rokoko_b200 import configs
+    u = configs.config0(seed=n_phon, n_phon=n_phon)
+    dov = u.durations if override else None
+    ref, ref_dur, ref_L, _ = oracle_model.infer(u.tokens, u.style, dov, bucket=32)
+    pcm, dur, L = gpu_ctx.infer(u.tokens, u.style, dov)
+    assert np.array_equal(dur, ref_dur), (dur, ref_dur)
+    assert L == ref_L
+    assert pcm.shape == ref.shape == (600 * L,)
+    report = []
+    for name, tol in STAGES:
+        g, o = gpu_ctx.stage(name), oracle_model.stage(name)
+        assert g is not None and o is not None, name
+        assert g.shape == o.shape, (name, g.shape, o.shape)
+        report.append((name, rel_l2(g, o), tol))
+    wav = rel_l2(pcm, ref)
+    msg = "\n".join(f"{n}: {r:.3e} (tol {t:.0e})" for n, r, t in report) + f"\naudio: {wav:.3e}"
+    print(msg)
+    for n, r, t in report:
+        assert r <= t, msg
+    assert wav <= 1e-3, msg

@@ -79,6 +79,23 @@ RK_API rk_status rk_conv1d_fprop(const float* x, const float* w, const float* bi
  * the start of a conv workspace: RK_OK or RK_ERR_DEVICE_TIMEOUT. */
 RK_API rk_status rk_conv1d_check(void* workspace, void* stream);
 
+/* rk_conv1d_fprop without a workspace argument and without any device
+ * allocation.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory where they need the convolution (inside a
+ * stream capture, under a host-owned memory pool, on a thread that must not
+ * block on the allocator, or within a fixed plugin budget).  Its scratch is one
+ * library-owned device array of RK_CONV_STATIC_SCRATCH_BYTES on each GPU that
+ * loads the library, kept until the process exits; shapes whose
+ * rk_conv1d_workspace_size exceeds it return RK_ERR_WORKSPACE.  The first call
+ * on a device looks up the array's address (make it before any stream
+ * capture).  All calls share the array: calls that can overlap on one GPU race
+ * and must be serialised by the caller.  Same arguments and results as
+ * rk_conv1d_fprop otherwise. */
+#define RK_CONV_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+RK_API rk_status rk_conv1d_fprop_static(const float* x, const float* w, const float* bias, float* y,
+                                        const float* residual, int C_in, int C_out, int T_in, int K, int stride,
+                                        int padding, int dilation, int precision, void* stream);
+
 /* ---- model context ------------------------------------------------------- */
 RK_API rk_status rk_create(int device, const rk_options* opts, rk_ctx** out);
 RK_API void rk_destroy(rk_ctx* ctx);

@@ -15,6 +15,8 @@ LIB_PATH = os.path.join(HERE, "librokoko_b200.so")
 RK_OK = 0
 RK_PRECISION_FP32 = 0
 RK_PRECISION_FP16 = 1
+RK_ERR_WORKSPACE = -2
+RK_CONV_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -40,6 +42,7 @@ SIGNATURES = [
     ("rk_conv1d_fprop", ctypes.c_int,
      [ctypes.c_void_p] * 5 + [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
     ("rk_conv1d_check", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ("rk_conv1d_fprop_static", ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
     ("rk_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(rk_options), ctypes.POINTER(ctypes.c_void_p)]),
     ("rk_destroy", None, [ctypes.c_void_p]),
     ("rk_load_weights_koko", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]),

@@ -56,6 +56,18 @@ def lib():
         L.orc_stft.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int]
         L.orc_istft.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int]
         L.orc_rand_ini.argtypes = [_f32p]
+        c_int, c_long, c_float = ctypes.c_int, ctypes.c_long, ctypes.c_float
+        L.orc_adain.argtypes = [_f32p, c_int, c_int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]
+        L.orc_layer_norm.argtypes = [_f32p, c_int, c_int, _f32p, _f32p, c_float, c_int, _f32p]
+        L.orc_durations_alignment.restype = c_int
+        L.orc_durations_alignment.argtypes = [_f32p, c_int, _i32p, _f32p, c_int]
+        L.orc_sigmoid_sum.argtypes = [_f32p, c_int, c_int, _f32p]
+        L.orc_lstm_gates.argtypes = [_f32p, _f32p, c_int, _f32p, _f32p]
+        L.orc_conv1d.argtypes = [_f32p, _f32p, _f32p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _f32p]
+        L.orc_convT_depthwise_k3s2.argtypes = [_f32p, _f32p, _f32p, c_int, c_int, _f32p]
+        L.orc_weight_norm.argtypes = [_f32p, _f32p, c_int, c_long, _f32p]
+        L.orc_gelu.argtypes = [_f32p, c_long, _f32p]
+        L.orc_softmax.argtypes = [_f32p, c_int, c_int, _f32p]
         _lib = L
     return _lib
 
@@ -163,3 +175,100 @@ def rand_ini():
     r = np.empty(9, np.float32)
     lib().orc_rand_ini(_fp(r))
     return r
+
+
+# ---- single-op restatements (pinned against the reference's own kernels by
+# tests/test_golden.py)
+
+def _c(a, dtype=np.float32):
+    return np.ascontiguousarray(a, dtype)
+
+
+def _fpn(a):
+    return None if a is None else _fp(a)
+
+
+def adain(x, norm_w, norm_b, gamma, beta, alpha=None):
+    """InstanceNorm + style affine (+ Snake) on x [T, C]."""
+    x, norm_w, norm_b, gamma, beta = map(_c, (x, norm_w, norm_b, gamma, beta))
+    alpha = None if alpha is None else _c(alpha)
+    T, C = x.shape
+    y = np.empty_like(x)
+    lib().orc_adain(_fp(x), T, C, _fp(norm_w), _fp(norm_b), _fp(gamma), _fp(beta), _fpn(alpha), _fp(y))
+    return y
+
+
+def layer_norm(x, gamma, beta, eps, ada=False):
+    x, gamma, beta = map(_c, (x, gamma, beta))
+    N, D = x.shape
+    y = np.empty_like(x)
+    lib().orc_layer_norm(_fp(x), N, D, _fp(gamma), _fp(beta), float(eps), int(bool(ada)), _fp(y))
+    return y
+
+
+def durations_alignment(dur, max_L=1 << 16):
+    """float durations [T] -> (int durations [T], L, alignment [T, L])."""
+    dur = _c(dur)
+    T = dur.shape[0]
+    idur = np.empty(T, np.int32)
+    L = lib().orc_durations_alignment(_fp(dur), T, _ip(idur), None, 0)
+    align = np.empty((T, L), np.float32)
+    lib().orc_durations_alignment(_fp(dur), T, _ip(idur), _fp(align), L)
+    return idur, L, align
+
+
+def sigmoid_sum(x):
+    x = _c(x)
+    y = np.empty(x.shape[0], np.float32)
+    lib().orc_sigmoid_sum(_fp(x), x.shape[0], x.shape[1], _fp(y))
+    return y
+
+
+def lstm_gates(gates, c_prev):
+    gates, c_prev = _c(gates), _c(c_prev)
+    H = c_prev.shape[0]
+    c = np.empty(H, np.float32)
+    h = np.empty(H, np.float32)
+    lib().orc_lstm_gates(_fp(gates), _fp(c_prev), H, _fp(c), _fp(h))
+    return c, h
+
+
+def conv1d(x, w, bias, stride=1, pad=0, dil=1):
+    """x [T_in, Ci], w [Co, Ci, K] -> y [T_out, Co]."""
+    x, w = _c(x), _c(w)
+    bias = None if bias is None else _c(bias)
+    T_in, Ci = x.shape
+    Co, _, K = w.shape
+    T_out = (T_in + 2 * pad - dil * (K - 1) - 1) // stride + 1
+    y = np.empty((T_out, Co), np.float32)
+    lib().orc_conv1d(_fp(x), _fp(w), _fpn(bias), Ci, Co, T_in, K, stride, pad, dil, _fp(y))
+    return y
+
+
+def conv_transpose_depthwise_k3s2(x, w, b):
+    x, w, b = map(_c, (x, w, b))
+    T, C = x.shape
+    y = np.empty((2 * T, C), np.float32)
+    lib().orc_convT_depthwise_k3s2(_fp(x), _fp(w), _fp(b), C, T, _fp(y))
+    return y
+
+
+def weight_norm(g, v):
+    g, v = _c(g), _c(v)
+    w = np.empty_like(v)
+    lib().orc_weight_norm(_fp(g), _fp(v), v.shape[0], v.size // v.shape[0], _fp(w))
+    return w
+
+
+def gelu(x):
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().orc_gelu(_fp(x), x.size, _fp(y))
+    return y
+
+
+def softmax(x):
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().orc_softmax(_fp(x), x.shape[0], x.shape[1], _fp(y))
+    return y

@@ -109,16 +109,19 @@ static Model* load_koko(const uint8_t* blob, size_t bytes, std::string& err) {
 // ------------------------------------------------------------- weight prep
 // Weight norm w = g * v / ||v|| over all dims but 0 (src/kernels.cu:327-356,
 // scripts/convert_v2.py:87-92).
-static Vec weight_norm(const Tensor& g, const Tensor& v) {
-    int rows = v.shape[0];
-    size_t fan = v.d.size() / rows;
-    Vec w(v.d.size());
+static void weight_norm_raw(const float* g, const float* v, int rows, size_t fan, float* w) {
     for (int o = 0; o < rows; o++) {
         double ss = 0;
-        for (size_t i = 0; i < fan; i++) ss += (double)v.d[o * fan + i] * v.d[o * fan + i];
+        for (size_t i = 0; i < fan; i++) ss += (double)v[o * fan + i] * v[o * fan + i];
         double nrm = std::max(std::sqrt(ss), 1e-12);
-        for (size_t i = 0; i < fan; i++) w[o * fan + i] = (float)((double)g.d[o] * v.d[o * fan + i] / nrm);
+        for (size_t i = 0; i < fan; i++) w[o * fan + i] = (float)((double)g[o] * v[o * fan + i] / nrm);
     }
+}
+
+static Vec weight_norm(const Tensor& g, const Tensor& v) {
+    int rows = v.shape[0];
+    Vec w(v.d.size());
+    weight_norm_raw(g.d.data(), v.d.data(), rows, v.d.size() / rows, w.data());
     return w;
 }
 
@@ -204,6 +207,22 @@ static Vec linear(Model& m, const Vec& x_in, int T, int in, const std::string& w
     return y;
 }
 
+// Conv1d core: y[T_out, Co] += sum_k x[t*stride - pad + k*dil] . B[k] with
+// B packed [K][Ci][Co] and zero padding outside [0, T_in).
+static void conv1d_raw(const float* x, int T_in, int Ci, const float* B, int Co, int K, int stride, int pad, int dil,
+                       int T_out, float* y) {
+    std::vector<const float*> ar(T_out);
+    std::vector<float*> cr(T_out);
+    for (int t = 0; t < T_out; t++) cr[t] = y + (size_t)t * Co;
+    for (int k = 0; k < K; k++) {
+        for (int t = 0; t < T_out; t++) {
+            int ti = t * stride - pad + k * dil;
+            ar[t] = (ti >= 0 && ti < T_in) ? x + (size_t)ti * Ci : nullptr;
+        }
+        gemm_rows_acc(T_out, Co, Ci, ar.data(), B + (size_t)k * Ci * Co, Co, cr.data());
+    }
+}
+
 // Conv1d on [T, C] activations (gemm_conv1d, src/rokoko.cpp:215-303):
 //   y = conv(x) + bias, or (conv(x) + residual) + bias.
 static Vec conv1d(Model& m, const Vec& x_in, int T_in, int Ci, const std::string& wname, const char* bname,
@@ -217,16 +236,7 @@ static Vec conv1d(Model& m, const Vec& x_in, int T_in, int Ci, const std::string
     const Vec* x = &x_in;
     if (m.fp16 && f16_act) { xr = x_in; round_f16(xr); x = &xr; }
     Vec y((size_t)T_out * Co, 0.f);
-    std::vector<const float*> ar(T_out);
-    std::vector<float*> cr(T_out);
-    for (int t = 0; t < T_out; t++) cr[t] = y.data() + (size_t)t * Co;
-    for (int k = 0; k < K; k++) {
-        for (int t = 0; t < T_out; t++) {
-            int ti = t * stride - pad + k * dil;
-            ar[t] = (ti >= 0 && ti < T_in) ? x->data() + (size_t)ti * Ci : nullptr;
-        }
-        gemm_rows_acc(T_out, Co, Ci, ar.data(), B.data() + (size_t)k * Ci * Co, Co, cr.data());
-    }
+    conv1d_raw(x->data(), T_in, Ci, B.data(), Co, K, stride, pad, dil, T_out, y.data());
     if (residual)
         for (size_t i = 0; i < y.size(); i++) y[i] += (*residual)[i];
     if (bname) {
@@ -307,11 +317,9 @@ static Vec style_fc(Model& m, const std::string& prefix, const float* s) {
 //   mean = sum x / T, var = sum x^2 / T - mean^2 (biased, single pass), eps 1e-5
 //   y = (1+gamma) (w (x-mean) inv_std + b) + beta, folded into scale*x + shift
 //   snake: y + sin(a y)^2 / a
-static Vec adain(Model& m, const Vec& x, int T, int C, const std::string& prefix, const float* style,
-                 const float* alpha) {
-    Vec fc = style_fc(m, prefix, style);
-    const float* nw = m.p(prefix + ".norm.weight");
-    const float* nb = m.p(prefix + ".norm.bias");
+//   gam = fc[0:C], bet = fc[C:2C] (the style FC output); alpha may be null.
+static void adain_apply(const float* x, int T, int C, const float* nw, const float* nb, const float* gam,
+                        const float* bet, const float* alpha, float* y) {
     std::vector<double> s(C, 0.0), sq(C, 0.0);
     for (int t = 0; t < T; t++)
         for (int c = 0; c < C; c++) { double v = x[(size_t)t * C + c]; s[c] += v; sq[c] += v * v; }
@@ -321,19 +329,39 @@ static Vec adain(Model& m, const Vec& x, int T, int C, const std::string& prefix
         double var_d = sq[c] / T - mean_d * mean_d;
         float mean = (float)mean_d;
         float inv_std = (float)(1.0 / std::sqrt(var_d + 1e-5));
-        float g = 1.0f + fc[c];
+        float g = 1.0f + gam[c];
         scale[c] = g * nw[c] * inv_std;
-        shift[c] = g * (nb[c] - nw[c] * mean * inv_std) + fc[C + c];
+        shift[c] = g * (nb[c] - nw[c] * mean * inv_std) + bet[c];
         if (alpha) { a[c] = alpha[c]; inva[c] = 1.0f / alpha[c]; }
     }
-    Vec y(x.size());
     for (int t = 0; t < T; t++)
         for (int c = 0; c < C; c++) {
             float v = scale[c] * x[(size_t)t * C + c] + shift[c];
             if (alpha) { float sn = sinf(a[c] * v); v = v + sn * sn * inva[c]; }
             y[(size_t)t * C + c] = v;
         }
+}
+
+static Vec adain(Model& m, const Vec& x, int T, int C, const std::string& prefix, const float* style,
+                 const float* alpha) {
+    Vec fc = style_fc(m, prefix, style);
+    Vec y(x.size());
+    adain_apply(x.data(), T, C, m.p(prefix + ".norm.weight"), m.p(prefix + ".norm.bias"), fc.data(), fc.data() + C,
+                alpha, y.data());
     return y;
+}
+
+// Depthwise ConvTranspose1d K3 s2 p1 op1 (src/kernels.cu:557-594): r [T, C] -> u [2T, C].
+static void dw_convT_k3s2(const float* r, int T, int C, const float* w, const float* b, float* u) {
+    for (int t = 0; t < 2 * T; t++)
+        for (int c = 0; c < C; c++) {
+            float acc = 0.f;
+            for (int k = 0; k < 3; k++) {
+                int tu = t + 1 - k;
+                if (tu >= 0 && tu % 2 == 0 && tu / 2 < T) acc += w[c * 3 + k] * r[(size_t)(tu / 2) * C + c];
+            }
+            u[(size_t)t * C + c] = acc + b[c];
+        }
 }
 
 // AdainResBlk1d (src/rokoko.cpp:583-643)
@@ -343,19 +371,8 @@ static Vec adain_resblk1d(Model& m, const Vec& x, int T, int din, int dout, cons
     Vec r = adain(m, x, T, din, pf + ".norm1", style, nullptr);
     lrelu_(r, 0.2f);
     if (upsample) {
-        // depthwise ConvTranspose1d K3 s2 p1 op1 (src/kernels.cu:557-594)
-        const float* w = m.p(pf + ".pool.weight_v");
-        const float* b = m.p(pf + ".pool.bias");
         Vec u((size_t)To * din);
-        for (int t = 0; t < To; t++)
-            for (int c = 0; c < din; c++) {
-                float acc = 0.f;
-                for (int k = 0; k < 3; k++) {
-                    int tu = t + 1 - k;
-                    if (tu >= 0 && tu % 2 == 0 && tu / 2 < T) acc += w[c * 3 + k] * r[(size_t)(tu / 2) * din + c];
-                }
-                u[(size_t)t * din + c] = acc + b[c];
-            }
+        dw_convT_k3s2(r.data(), T, din, m.p(pf + ".pool.weight_v"), m.p(pf + ".pool.bias"), u.data());
         r.swap(u);
     }
     r = conv1d(m, r, To, din, pf + ".conv1.weight_v", (pf + ".conv1.bias").c_str(), 1, 1, 1, nullptr, true);
@@ -684,6 +701,58 @@ static Vec decode(Model& m, const Vec& asr, const Vec& f0, const Vec& nn, const 
 
 // ------------------------------------------------------------- front half
 // ALBERT (src/rokoko.cpp:335-408)
+// gelu_new / tanh approximation (src/kernels.cu:151-158)
+static inline float gelu_new(float v) {
+    float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(inner));
+}
+
+// Row softmax in place (src/kernels.cu:189-225): max-subtracted expf, sum in double.
+static void softmax_row(float* p, int n) {
+    float mx = -1e30f;
+    for (int j = 0; j < n; j++) mx = std::max(mx, p[j]);
+    double se = 0;
+    for (int j = 0; j < n; j++) { p[j] = expf(p[j] - mx); se += p[j]; }
+    float inv = (float)(1.0 / se);
+    for (int j = 0; j < n; j++) p[j] = p[j] * inv;
+}
+
+// AdaLayerNorm rows (src/kernels.cu:513-548): y = (1+gam) LN(x) + bet, no affine of its own.
+static void ada_layer_norm_rows(float* x, int N, int D, const float* gam, const float* bet, float eps) {
+    for (int t = 0; t < N; t++) {
+        float* row = x + (size_t)t * D;
+        double sm = 0;
+        for (int d = 0; d < D; d++) sm += row[d];
+        float mean = (float)(sm / D);
+        double vs = 0;
+        for (int d = 0; d < D; d++) { double df = (double)row[d] - mean; vs += df * df; }
+        float inv = (float)(1.0 / std::sqrt(vs / D + eps));
+        for (int d = 0; d < D; d++) row[d] = (1.0f + gam[d]) * ((row[d] - mean) * inv) + bet[d];
+    }
+}
+
+// One LSTM step's gate activations (src/kernels.cu:976-997): g [4H] = i, f, g, o.
+static void lstm_cell(const float* g, float* c, float* h, int H) {
+    for (int i = 0; i < H; i++) {
+        float ii = 1.0f / (1.0f + expf(-g[i]));
+        float ff = 1.0f / (1.0f + expf(-g[H + i]));
+        float gg = tanhf(g[2 * H + i]);
+        float oo = 1.0f / (1.0f + expf(-g[3 * H + i]));
+        float cc = ff * c[i] + ii * gg;
+        c[i] = cc;
+        h[i] = oo * tanhf(cc);
+    }
+}
+
+// Duration head: sum of sigmoids over D logits (src/kernels.cu:643-662), then
+// round half to even and clamp to >= 1 (src/kernels.cu:1457-1479).
+static float sigmoid_sum_row(const float* x, int D) {
+    double sm = 0;
+    for (int d = 0; d < D; d++) sm += 1.0f / (1.0f + expf(-x[d]));
+    return (float)sm;
+}
+static inline int round_clamp_duration(float d) { return std::max(1, (int)std::nearbyint(d)); }
+
 static Vec albert(Model& m, const int* tok, int T) {
     const float* we = m.p("bert.embeddings.word_embeddings.weight");
     const float* pe = m.p("bert.embeddings.position_embeddings.weight");
@@ -704,19 +773,15 @@ static Vec albert(Model& m, const int* tok, int T) {
         parallel_for(12, [&](int hd) {
             Vec p((size_t)T);
             for (int i = 0; i < T; i++) {
-                float mx = -1e30f;
                 for (int j = 0; j < T; j++) {
                     float acc = 0.f;
                     for (int d = 0; d < 64; d++) acc += q[(size_t)i * 768 + hd * 64 + d] * k[(size_t)j * 768 + hd * 64 + d];
                     p[j] = acc * 0.125f;
-                    mx = std::max(mx, p[j]);
                 }
-                double se = 0;
-                for (int j = 0; j < T; j++) { p[j] = expf(p[j] - mx); se += p[j]; }
-                float inv = (float)(1.0 / se);
+                softmax_row(p.data(), T);
                 for (int d = 0; d < 64; d++) {
                     float acc = 0.f;
-                    for (int j = 0; j < T; j++) acc += (p[j] * inv) * v[(size_t)j * 768 + hd * 64 + d];
+                    for (int j = 0; j < T; j++) acc += p[j] * v[(size_t)j * 768 + hd * 64 + d];
                     ctx[(size_t)i * 768 + hd * 64 + d] = acc;
                 }
             }
@@ -725,10 +790,7 @@ static Vec albert(Model& m, const int* tok, int T) {
         for (size_t i = 0; i < h.size(); i++) h[i] = h[i] + at[i];
         layer_norm_rows(h, T, 768, m.p(a + ".attention.LayerNorm.weight"), m.p(a + ".attention.LayerNorm.bias"), 1e-12f);
         Vec f = linear(m, h, T, 768, a + ".ffn.weight", (a + ".ffn.bias").c_str(), true);
-        for (auto& vv : f) {  // gelu_new (src/kernels.cu:151-158)
-            float inner = 0.7978845608028654f * (vv + 0.044715f * vv * vv * vv);
-            vv = 0.5f * vv * (1.0f + tanhf(inner));
-        }
+        for (auto& vv : f) vv = gelu_new(vv);
         Vec f2 = linear(m, f, T, 2048, a + ".ffn_output.weight", (a + ".ffn_output.bias").c_str(), true);
         for (size_t i = 0; i < h.size(); i++) h[i] = h[i] + f2[i];
         layer_norm_rows(h, T, 768, m.p(a + ".full_layer_layer_norm.weight"), m.p(a + ".full_layer_layer_norm.bias"), 1e-12f);
@@ -767,16 +829,8 @@ static Vec bilstm(Model& m, const Vec& x, int T, int in, const std::string& pf) 
                 for (int k = 0; k < H; k++) acc += wr[k] * h[k];
                 g[gi] = ig[(size_t)t * G + gi] + acc;
             }
-            for (int i = 0; i < H; i++) {
-                float ii = 1.0f / (1.0f + expf(-g[i]));
-                float ff = 1.0f / (1.0f + expf(-g[H + i]));
-                float gg = tanhf(g[2 * H + i]);
-                float oo = 1.0f / (1.0f + expf(-g[3 * H + i]));
-                float cc = ff * c[i] + ii * gg;
-                c[i] = cc;
-                h[i] = oo * tanhf(cc);
-                out[(size_t)t * 512 + rev * H + i] = h[i];
-            }
+            lstm_cell(g.data(), c.data(), h.data(), H);
+            std::memcpy(&out[(size_t)t * 512 + rev * H], h.data(), H * sizeof(float));
         }
     };
     std::thread th([&] { dir(1); });
@@ -820,17 +874,7 @@ static InferOut infer(Model& m, const int* tok, int T, const float* style, const
     for (int li = 0; li < 3; li++) {
         Vec l = bilstm(m, cat, T, 640, "predictor.text_encoder.lstms." + std::to_string(2 * li));
         Vec fc = style_fc(m, "predictor.text_encoder.lstms." + std::to_string(2 * li + 1), s_pr);
-        // AdaLayerNorm (src/kernels.cu:513-548)
-        for (int t = 0; t < T; t++) {
-            float* row = l.data() + (size_t)t * 512;
-            double sm = 0;
-            for (int d = 0; d < 512; d++) sm += row[d];
-            float mean = (float)(sm / 512);
-            double vs = 0;
-            for (int d = 0; d < 512; d++) { double df = (double)row[d] - mean; vs += df * df; }
-            float inv = (float)(1.0 / std::sqrt(vs / 512 + 1e-5));
-            for (int d = 0; d < 512; d++) row[d] = (1.0f + fc[d]) * ((row[d] - mean) * inv) + fc[512 + d];
-        }
+        ada_layer_norm_rows(l.data(), T, 512, fc.data(), fc.data() + 512, 1e-5f);
         fill_cat(l);
     }
     m.dump("dur_enc", cat);
@@ -840,11 +884,9 @@ static InferOut infer(Model& m, const int* tok, int T, const float* style, const
     InferOut out;
     out.dur.resize(T);
     Vec durf(T);
-    for (int t = 0; t < T; t++) {  // sigmoid_sum + round_clamp (src/kernels.cu:643-662, 1457-1479)
-        double sm = 0;
-        for (int d = 0; d < 50; d++) sm += 1.0f / (1.0f + expf(-pj[(size_t)t * 50 + d]));
-        durf[t] = (float)sm;
-        out.dur[t] = std::max(1, (int)std::nearbyint(durf[t]));
+    for (int t = 0; t < T; t++) {
+        durf[t] = sigmoid_sum_row(&pj[(size_t)t * 50], 50);
+        out.dur[t] = round_clamp_duration(durf[t]);
     }
     m.dump("dur_float", durf);
     // out.dur keeps the predicted durations; the alignment uses the override when given
@@ -968,5 +1010,67 @@ void orc_sinegen(const float* f0, int L2, const float* lw, const float* lb, floa
 void orc_stft(const float* x, int T, float* har, int T2) { stft(x, T, har, T2); }
 void orc_istft(const float* c, int T2, float* y, int T_audio) { istft(c, T2, y, T_audio); }
 void orc_rand_ini(float* ri) { rand_ini9(ri); }
+
+void orc_adain(const float* x, int T, int C, const float* nw, const float* nb, const float* gam, const float* bet,
+               const float* alpha, float* y) {
+    adain_apply(x, T, C, nw, nb, gam, bet, alpha, y);
+}
+void orc_layer_norm(const float* x, int N, int D, const float* g, const float* b, float eps, int ada, float* y) {
+    std::memcpy(y, x, sizeof(float) * (size_t)N * D);
+    if (ada) ada_layer_norm_rows(y, N, D, g, b, eps);
+    else {
+        Vec v(y, y + (size_t)N * D);
+        layer_norm_rows(v, N, D, g, b, eps);
+        std::memcpy(y, v.data(), sizeof(float) * v.size());
+    }
+}
+// durations [T] float -> int durations, total L; alignment [T, L] (if non-null)
+int orc_durations_alignment(const float* dur, int T, int* idur, float* align, int max_L) {
+    int L = 0;
+    for (int t = 0; t < T; t++) { idur[t] = round_clamp_duration(dur[t]); L += idur[t]; }
+    if (align && L <= max_L) {
+        std::memset(align, 0, sizeof(float) * (size_t)T * L);
+        int off = 0;
+        for (int t = 0; t < T; t++) {
+            for (int r = 0; r < idur[t]; r++) align[(size_t)t * L + off + r] = 1.0f;
+            off += idur[t];
+        }
+    }
+    return L;
+}
+void orc_sigmoid_sum(const float* x, int N, int D, float* y) {
+    for (int n = 0; n < N; n++) y[n] = sigmoid_sum_row(x + (size_t)n * D, D);
+}
+void orc_lstm_gates(const float* g, const float* c_prev, int H, float* c_out, float* h_out) {
+    std::memcpy(c_out, c_prev, sizeof(float) * H);
+    lstm_cell(g, c_out, h_out, H);
+}
+// w [Co, Ci, K] (PyTorch layout), x [T_in, Ci] -> y [T_out, Co]; bias may be null
+void orc_conv1d(const float* x, const float* w, const float* bias, int Ci, int Co, int T_in, int K, int stride, int pad,
+                int dil, float* y) {
+    Vec B((size_t)K * Ci * Co);
+    for (int co = 0; co < Co; co++)
+        for (int ci = 0; ci < Ci; ci++)
+            for (int k = 0; k < K; k++) B[((size_t)k * Ci + ci) * Co + co] = w[((size_t)co * Ci + ci) * K + k];
+    const int T_out = (T_in + 2 * pad - dil * (K - 1) - 1) / stride + 1;
+    std::memset(y, 0, sizeof(float) * (size_t)T_out * Co);
+    conv1d_raw(x, T_in, Ci, B.data(), Co, K, stride, pad, dil, T_out, y);
+    if (bias)
+        for (int t = 0; t < T_out; t++)
+            for (int c = 0; c < Co; c++) y[(size_t)t * Co + c] += bias[c];
+}
+void orc_convT_depthwise_k3s2(const float* x, const float* w, const float* b, int C, int T_in, float* y) {
+    dw_convT_k3s2(x, T_in, C, w, b, y);
+}
+void orc_weight_norm(const float* g, const float* v, int rows, long fan, float* w) {
+    weight_norm_raw(g, v, rows, (size_t)fan, w);
+}
+void orc_gelu(const float* x, long n, float* y) {
+    for (long i = 0; i < n; i++) y[i] = gelu_new(x[i]);
+}
+void orc_softmax(const float* x, int N, int D, float* y) {
+    std::memcpy(y, x, sizeof(float) * (size_t)N * D);
+    for (int r = 0; r < N; r++) softmax_row(y + (size_t)r * D, D);
+}
 
 }  // extern "C"

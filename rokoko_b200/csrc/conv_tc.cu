@@ -5,20 +5,34 @@
 // im2col + GEMM fallback (src/rokoko.cpp:286-302) and the GEMM + atomic col2im
 // ConvTranspose1d (src/rokoko.cpp:308-329, src/kernels.cu:1141-1173).
 //
-// CTA = 6 warps, one 128-row x NB-column output tile, two CTAs per SM:
-//   warp 0   TMA producer.  Per 64-channel block it loads ONE activation tile
-//            of H = 128 + halo rows (halo = max tap offset - min tap offset;
-//            TMA zero-fills rows outside [0, T_in), i.e. the padding), and per
-//            (channel block, tap) one weight tile.
-//   warp 1   owns TMEM; one elected thread issues tcgen05.mma (M=128, N=NB,
-//            K=16 each, 4 per 64-channel block, x3 in split mode).  Tap k
-//            reuses the activation tile through a descriptor whose start is
-//            shifted by (tap_off[k] - min_off) rows, so the activations cross
-//            L2 -> SMEM once per channel block instead of once per tap.
-//   warps 2-5 epilogue: tcgen05.ld 32 columns, transpose through shared memory
-//            and process the tile as coalesced float4 row segments: bias,
+// Orientation: the weights are the MMA's M = 128 side (output channels) and
+// the activations the N side (BN = 64, 128 or 256 time rows), so one weight
+// tile streamed from L2 feeds BN rows of output; at BN = 256 the tensor pipe
+// runs near its peak with a two-deep weight ring (measured on B200: the same
+// stream at N = 128 saturates the L2 -> SMEM path first).
+//
+// Persistent kernel: grid = min(tiles, SMs), one CTA per SM; CTA b runs tiles
+// b, b + grid, ... (time fastest, so neighbouring CTAs share the weight tile in
+// L2).  10 warps, specialised:
+//   warp 0   TMA producer.  Per tile and 64-channel block it loads ONE
+//            activation tile of BN + halo rows (two boxes; halo = max tap
+//            offset - min tap offset; TMA zero-fills rows outside [0, T_in),
+//            i.e. the padding) into a 2-deep ring, and per (channel block, tap)
+//            one 128-row weight tile into a 2..8-deep ring.
+//   warp 1   owns TMEM (two accumulators of BN columns); one elected thread
+//            issues tcgen05.mma (M=128, N=BN, K=16; 4 per 64-channel block, x3
+//            in split mode).  Tap k reads the activation tile through a
+//            descriptor whose start is shifted by (tap_off[k] - min_off) rows,
+//            so activations cross L2 -> SMEM once per channel block.
+//   warps 2-9 epilogue of the previous tile while the MMAs of the next one run:
+//            warp w reads TMEM lanes 32(w%4).. = output channels (two warps per
+//            lane quarter split the tile's row pairs), tcgen05.ld
+//            brings 32 time rows per thread, and every row is stored as 32
+//            consecutive channels (one 128-byte segment per warp): bias,
 //            residual, accumulate, scale, store, plus per-channel sum and
-//            sum-of-squares partials for the next InstanceNorm.
+//            sum-of-squares partials (64-row parts) for the next InstanceNorm.
+// Every wait is bounded (ptx.cuh); a timeout records an error code and the
+// roles drain and return, so a protocol fault is an error status, not a hang.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -29,23 +43,24 @@ namespace rk {
 
 namespace {
 
-constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int MAX_HPAD = 184;       // halo tile rows (128 + halo <= 178, padded to 8)
-constexpr int STAGE_PAD = 36;       // epilogue staging row pitch (floats)
+constexpr int X_STAGES = 2;
+constexpr int MAX_W_STAGES = 8;
+constexpr size_t SMEM_LIMIT = 227 * 1024 - 1024;  // dynamic bytes; leaves room for the static barriers
 
-template <int NB, bool SPLIT>
+template <int BN, bool SPLIT>
 struct Cfg {
     static constexpr int NPL = SPLIT ? 2 : 1;
-    static constexpr uint32_t B_BYTES = NB * BK * 2;          // one plane
-    static constexpr uint32_t B_STAGE = NPL * B_BYTES;
-    // budget: two CTAs per SM (<= ~113 KB each)
-    static constexpr int B_STAGES = SPLIT ? 2 : 4;
-    static constexpr uint32_t TMEM_COLS = NB < 32 ? 32 : NB;
-    static constexpr size_t smem_bytes(int H_pad) {
-        return 1024 + (size_t)NPL * H_pad * 128 + (size_t)B_STAGES * B_STAGE;
+    static constexpr uint32_t W_PLANE = CONV_W_ROWS * BK * 2;   // 16 KB
+    static constexpr uint32_t W_STAGE = NPL * W_PLANE;
+    static size_t x_stage(int box) { return (size_t)NPL * 2 * box * 128; }
+    static size_t fixed_bytes(int box) { return 1024 + X_STAGES * x_stage(box); }
+    static int w_stages(int box) {
+        if (fixed_bytes(box) >= SMEM_LIMIT) return 0;
+        const int n = (int)((SMEM_LIMIT - fixed_bytes(box)) / W_STAGE);
+        return n > MAX_W_STAGES ? MAX_W_STAGES : n;
     }
-    static constexpr size_t SMEM_MAX = 1024 + (size_t)NPL * MAX_HPAD * 128 + (size_t)B_STAGES * B_STAGE;
+    static size_t smem_bytes(int box, int ws) { return fixed_bytes(box) + (size_t)ws * W_STAGE; }
 };
 
 // gelu_new: 0.5 v (1 + tanh(0.7978845608 (v + 0.044715 v^3)))
@@ -54,40 +69,55 @@ __device__ __forceinline__ float gelu_tanh(float v) {
     return 0.5f * v * (1.0f + tanhf(inner));
 }
 
-template <int NB, bool SPLIT>
-__global__ void __launch_bounds__(192, 2)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA_hi, const __grid_constant__ CUtensorMap tmA_lo,
-                   const __grid_constant__ CUtensorMap tmB_hi, const __grid_constant__ CUtensorMap tmB_lo,
-                   const __grid_constant__ ConvArgs args) {
-    using C = Cfg<NB, SPLIT>;
-    constexpr int BS = C::B_STAGES;
+struct Tiles {
+    int tiles_t, tiles_c, n_tiles;
+    __device__ void decode(int t, int& t_tile, int& c_tile, int& phase) const {
+        phase = t / (tiles_t * tiles_c);
+        const int rem = t - phase * tiles_t * tiles_c;
+        c_tile = rem / tiles_t;
+        t_tile = rem - c_tile * tiles_t;
+    }
+};
+
+template <int BN, bool SPLIT>
+__global__ void __launch_bounds__(320, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmX_hi, const __grid_constant__ CUtensorMap tmX_lo,
+                   const __grid_constant__ CUtensorMap tmW_hi, const __grid_constant__ CUtensorMap tmW_lo,
+                   const __grid_constant__ ConvArgs args, int n_phases, int WS) {
+    using C = Cfg<BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t a_full, a_empty, acc_bar;
-    __shared__ __align__(8) uint64_t b_full[BS], b_empty[BS];
+    __shared__ __align__(8) uint64_t x_full[X_STAGES], x_empty[X_STAGES];
+    __shared__ __align__(8) uint64_t w_full[MAX_W_STAGES], w_empty[MAX_W_STAGES];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
     __shared__ uint32_t tmem_base_sh;
+    __shared__ int epi_dead;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m_tile = blockIdx.x, n_tile = blockIdx.y, phase = blockIdx.z;
-    const int m0 = m_tile * BM, n0 = n_tile * NB;
-    const int H_pad = args.h_pad;
-    const uint32_t a_plane = (uint32_t)H_pad * 128;
-    uint8_t* a_buf = smem;                                   // [plane][H_pad rows][128 B]
-    uint8_t* b_buf = smem + C::NPL * a_plane;                // [stage][plane][NB rows][128 B]
+    const int box = args.act_box;
+    const uint32_t x_plane = (uint32_t)(2 * box) * 128;
+    const uint32_t x_stage = C::NPL * x_plane;
+    uint8_t* x_buf = smem;                                       // [stage][plane][2*box rows][128 B]
+    uint8_t* w_buf = smem + (size_t)X_STAGES * x_stage;          // [stage][plane][128 rows][128 B]
     const int KB = args.kblocks, TAPS = args.taps;
+    Tiles g;
+    g.tiles_t = (args.M + BN - 1) / BN;
+    g.tiles_c = (args.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS;
+    g.n_tiles = g.tiles_t * g.tiles_c * n_phases;
 
     if (warp == 0 && lane == 0) {
-        mbar_init(&a_full, 1);
-        mbar_init(&a_empty, 1);
-        mbar_init(&acc_bar, 1);
-        for (int s = 0; s < BS; s++) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
+        for (int s = 0; s < X_STAGES; s++) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
+        for (int s = 0; s < WS; s++) { mbar_init(&w_full[s], 1); mbar_init(&w_empty[s], 1); }
+        for (int s = 0; s < 2; s++) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 8); }
+        mbar_init(&drain_bar, 1);
+        epi_dead = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&tmA_hi);
-        tma_prefetch_desc(&tmB_hi);
-        if (SPLIT) { tma_prefetch_desc(&tmA_lo); tma_prefetch_desc(&tmB_lo); }
+        tma_prefetch_desc(&tmX_hi);
+        tma_prefetch_desc(&tmW_hi);
+        if (SPLIT) { tma_prefetch_desc(&tmX_lo); tma_prefetch_desc(&tmW_lo); }
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+        tmem_alloc(&tmem_base_sh, 2 * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -98,195 +128,219 @@ __global__ void __launch_bounds__(192, 2)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int brow = phase * args.b_phase_rows + n0;
-            const int arow = m0 + args.a_off + args.min_off;
-            int bit = 0;
+            uint32_t xi = 0, wi = 0;
             bool alive = true;
-            for (int kb = 0; kb < KB && alive; kb++) {
-                // the single activation buffer is free once every MMA of the previous block completed
-                if (!mbar_wait(&a_empty, ((uint32_t)kb & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&a_full, C::NPL * a_plane);
-                tma_load_2d(a_buf, &tmA_hi, &a_full, kb * BK, arow);
-                if (SPLIT) tma_load_2d(a_buf + a_plane, &tmA_lo, &a_full, kb * BK, arow);
-                for (int tap = 0; tap < TAPS; tap++, bit++) {
-                    const int s = bit % BS;
-                    const uint32_t round = (uint32_t)(bit / BS);
-                    if (!mbar_wait(&b_empty[s], (round & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) {
-                        alive = false;
-                        break;
+            for (int t = blockIdx.x; t < g.n_tiles && alive; t += gridDim.x) {
+                int t_tile, c_tile, phase;
+                g.decode(t, t_tile, c_tile, phase);
+                const int wrow = phase * args.b_phase_rows + c_tile * CONV_W_ROWS;
+                const int xrow = t_tile * BN + args.a_off + args.min_off;
+                for (int kb = 0; kb < KB && alive; kb++, xi++) {
+                    const uint32_t sx = xi % X_STAGES, rx = xi / X_STAGES;
+                    if (!mbar_wait(&x_empty[sx], (rx & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) { alive = false; break; }
+                    uint8_t* xb = x_buf + (size_t)sx * x_stage;
+                    mbar_arrive_expect_tx(&x_full[sx], x_stage);
+                    tma_load_2d(xb, &tmX_hi, &x_full[sx], kb * BK, xrow);
+                    tma_load_2d(xb + (size_t)box * 128, &tmX_hi, &x_full[sx], kb * BK, xrow + box);
+                    if (SPLIT) {
+                        tma_load_2d(xb + x_plane, &tmX_lo, &x_full[sx], kb * BK, xrow);
+                        tma_load_2d(xb + x_plane + (size_t)box * 128, &tmX_lo, &x_full[sx], kb * BK, xrow + box);
                     }
-                    uint8_t* sb = b_buf + (size_t)s * C::B_STAGE;
-                    mbar_arrive_expect_tx(&b_full[s], C::B_STAGE);
-                    const int bx = (tap * KB + kb) * BK;
-                    tma_load_2d(sb, &tmB_hi, &b_full[s], bx, brow);
-                    if (SPLIT) tma_load_2d(sb + C::B_BYTES, &tmB_lo, &b_full[s], bx, brow);
+                    for (int tap = 0; tap < TAPS; tap++, wi++) {
+                        const uint32_t sw = wi % (uint32_t)WS, rw = wi / (uint32_t)WS;
+                        if (!mbar_wait(&w_empty[sw], (rw & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) {
+                            alive = false;
+                            break;
+                        }
+                        uint8_t* wb = w_buf + (size_t)sw * C::W_STAGE;
+                        mbar_arrive_expect_tx(&w_full[sw], C::W_STAGE);
+                        const int wx = (tap * KB + kb) * BK;
+                        tma_load_2d(wb, &tmW_hi, &w_full[sw], wx, wrow);
+                        if (SPLIT) tma_load_2d(wb + C::W_PLANE, &tmW_lo, &w_full[sw], wx, wrow);
+                    }
                 }
             }
+            // the last copy issued into each stage has landed (instant unless a consumer gave up)
+            for (uint32_t k = xi > (uint32_t)X_STAGES ? xi - X_STAGES : 0u; k < xi; k++)
+                mbar_wait(&x_full[k % X_STAGES], (k / X_STAGES) & 1u, args.err, RK_DEV_TIMEOUT_DRAIN);
+            for (uint32_t k = wi > (uint32_t)WS ? wi - WS : 0u; k < wi; k++)
+                mbar_wait(&w_full[k % WS], (k / WS) & 1u, args.err, RK_DEV_TIMEOUT_DRAIN);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_f16(BM, NB, SPLIT);
-            const uint32_t a_hi = smem_u32(a_buf), a_lo = a_hi + a_plane;
-            int bit = 0;
+            constexpr uint32_t idesc = umma_idesc_f16(CONV_W_ROWS, BN, SPLIT);
+            uint32_t xi = 0, wi = 0, tl = 0;
             bool alive = true;
-            for (int kb = 0; kb < KB && alive; kb++) {
-                if (!mbar_wait(&a_full, (uint32_t)kb & 1u, args.err, RK_DEV_TIMEOUT_FULL)) break;
+            for (int t = blockIdx.x; t < g.n_tiles && alive; t += gridDim.x, tl++) {
+                const uint32_t acc = tl & 1u, ru = tl >> 1;
+                if (!mbar_wait(&acc_empty[acc], (ru & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) break;
                 tc_fence_after();
-                for (int tap = 0; tap < TAPS; tap++, bit++) {
-                    const int s = bit % BS;
-                    const uint32_t round = (uint32_t)(bit / BS);
-                    if (!mbar_wait(&b_full[s], round & 1u, args.err, RK_DEV_TIMEOUT_FULL)) {
-                        alive = false;
-                        break;
-                    }
+                const uint32_t d_tmem = tmem + acc * BN;
+                for (int kb = 0; kb < KB && alive; kb++, xi++) {
+                    const uint32_t sx = xi % X_STAGES, rx = xi / X_STAGES;
+                    if (!mbar_wait(&x_full[sx], rx & 1u, args.err, RK_DEV_TIMEOUT_FULL)) { alive = false; break; }
                     tc_fence_after();
-                    const uint32_t shift = (uint32_t)(args.tap_off[tap] - args.min_off) * 128u;
-                    const uint32_t b_hi = smem_u32(b_buf + (size_t)s * C::B_STAGE), b_lo = b_hi + C::B_BYTES;
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++) {
-                        const uint64_t dah = sw128_kmajor_desc(a_hi + shift + kk * 32, args.desc_mode);
-                        const uint64_t dbh = sw128_kmajor_desc(b_hi + kk * 32, 0);
-                        umma_f16(tmem, dah, dbh, idesc, (kb > 0 || tap > 0 || kk > 0) ? 1u : 0u);
-                        if (SPLIT) {
-                            umma_f16(tmem, dah, sw128_kmajor_desc(b_lo + kk * 32, 0), idesc, 1u);
-                            umma_f16(tmem, sw128_kmajor_desc(a_lo + shift + kk * 32, args.desc_mode), dbh, idesc,
-                                     1u);
+                    const uint32_t x_hi = smem_u32(x_buf + (size_t)sx * x_stage), x_lo = x_hi + x_plane;
+                    for (int tap = 0; tap < TAPS; tap++, wi++) {
+                        const uint32_t sw = wi % (uint32_t)WS, rw = wi / (uint32_t)WS;
+                        if (!mbar_wait(&w_full[sw], rw & 1u, args.err, RK_DEV_TIMEOUT_FULL)) {
+                            alive = false;
+                            break;
                         }
+                        tc_fence_after();
+                        const uint32_t shift = (uint32_t)(args.tap_off[tap] - args.min_off) * 128u;
+                        const uint32_t w_hi = smem_u32(w_buf + (size_t)sw * C::W_STAGE), w_lo = w_hi + C::W_PLANE;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++) {
+                            const uint64_t dwh = sw128_kmajor_desc(w_hi + kk * 32, 0);
+                            const uint64_t dxh = sw128_kmajor_desc(x_hi + shift + kk * 32, args.desc_mode);
+                            umma_f16(d_tmem, dwh, dxh, idesc, (kb > 0 || tap > 0 || kk > 0) ? 1u : 0u);
+                            if (SPLIT) {
+                                umma_f16(d_tmem, dwh, sw128_kmajor_desc(x_lo + shift + kk * 32, args.desc_mode),
+                                         idesc, 1u);
+                                umma_f16(d_tmem, sw128_kmajor_desc(w_lo + kk * 32, 0), dxh, idesc, 1u);
+                            }
+                        }
+                        umma_commit(&w_empty[sw]);
                     }
-                    umma_commit(&b_empty[s]);
+                    umma_commit(&x_empty[sx]);
                 }
-                umma_commit(&a_empty);
+                umma_commit(&acc_full[acc]);
             }
-            umma_commit(&acc_bar);
-            // every MMA this thread issued has completed once acc_bar flips
-            mbar_wait(&acc_bar, 0, args.err, RK_DEV_TIMEOUT_DRAIN);
+            // drain: every MMA this thread issued has completed once this commit lands
+            umma_commit(&drain_bar);
+            mbar_wait(&drain_bar, 0, args.err, RK_DEV_TIMEOUT_DRAIN);
+            tc_fence_before();
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 2..5)
-        const int wq = warp & 3;  // TMEM lane quarter this warp may access
-        const bool ok = mbar_wait(&acc_bar, 0, args.err, RK_DEV_TIMEOUT_ACC);
-        tc_fence_after();
-        // every MMA has completed, so the operand buffers are free: stage through them
-        float* stg = reinterpret_cast<float*>(smem) + (size_t)wq * 32 * STAGE_PAD;
-        float* red = reinterpret_cast<float*>(smem) + 4 * 32 * STAGE_PAD;  // [2][4][NB]
+        // ------------------------------------------------ epilogue (warps 2..9)
+        // TMEM lane quarter = warp % 4 (the hardware rule); the two warps of a
+        // quarter split the tile's 64-row pairs of chunks between them.
+        const int wq = warp & 3;
+        const int half = (warp - 2) >> 2;
         const bool want_stats = args.stats != nullptr;
-        const int cg = lane & 7;        // 4-column group within the 32-column chunk
-        const int rsub = lane >> 3;     // row within a group of 4
+        const int parts_per_phase = (args.M + STATS_ROWS - 1) / STATS_ROWS;
+        uint32_t tl = 0;
+        for (int t = blockIdx.x; t < g.n_tiles; t += gridDim.x, tl++) {
+            int t_tile, c_tile, phase;
+            g.decode(t, t_tile, c_tile, phase);
+            const int m0 = t_tile * BN;
+            const int co = c_tile * CONV_W_ROWS + wq * 32 + lane;
+            const bool co_ok = co < args.C_out;
+            const float bias_v = (args.bias && co_ok) ? args.bias[co] : 0.0f;
+            const uint32_t acc = tl & 1u, ru = tl >> 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], ru & 1u, args.err, RK_DEV_TIMEOUT_ACC));
+            tc_fence_after();
+            if (!ok && lane == 0) epi_dead = 1;
+            const uint32_t s_tmem = tmem + acc * BN + ((uint32_t)(wq * 32) << 16);
+            // Common case, branch-free so the 32 rows of a chunk interleave: plain
+            // residual (no row shift), no activation, no accumulator input, no
+            // duplicated row, and every row of the chunk inside the output.
+            const bool fast_conv = co_ok && !args.act && !args.acc_in && args.res_shift == 0 && args.dup_src_row < 0;
 #pragma unroll 1
-        for (int c = 0; c < NB / 32; c++) {
-            float v[32];
-            tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(c * 32), v);
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(stg + lane * STAGE_PAD + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            __syncwarp();
-            const int co = n0 + c * 32 + cg * 4;
-            const int ncol = min(4, args.C_out - co);
-            float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (args.bias && ncol > 0) {
-                bias4.x = args.bias[co];
-                if (ncol > 1) bias4.y = args.bias[co + 1];
-                if (ncol > 2) bias4.z = args.bias[co + 2];
-                if (ncol > 3) bias4.w = args.bias[co + 3];
-            }
-            float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = s4;
-#pragma unroll 2
-            for (int i = 0; i < 8; i++) {
-                const int r = i * 4 + rsub;
-                const int m = m0 + wq * 32 + r;
-                const int out_row = m * args.o_stride + args.o_off + phase * args.o_phase_step;
-                const bool valid = ok && m < args.M && out_row >= args.o_min && out_row < args.T_out && ncol > 0;
-                if (!valid) continue;
-                const float4 a = *reinterpret_cast<const float4*>(stg + r * STAGE_PAD + cg * 4);
-                const bool vec = ncol == 4;
-                // main row, then (reflection pad) the duplicate written to row 0
-                for (int pass = 0; pass < 2; pass++) {
-                    int orow = out_row, rrow = out_row >> args.res_shift;
-                    if (pass == 1) {
-                        if (out_row != args.dup_src_row) break;
-                        orow = 0;
-                        rrow = 0;
-                    }
-                    float4 o = a;
+            for (int pp = half; pp < (ok ? BN / 64 : 0); pp += 2) {
+                float s = 0.f, q = 0.f;
+                const int mp = m0 + pp * 64;
+                const int orow_p = mp * args.o_stride + args.o_off + phase * args.o_phase_step;
+                const int orow_last = orow_p + 63 * args.o_stride;
+                // warp-uniform: tcgen05.ld below is a .sync.aligned instruction, so every lane
+                // of the warp must take the same path (lanes past C_out take the general one)
+                const bool fast = __all_sync(0xffffffffu, fast_conv && mp + 63 < args.M && orow_p >= args.o_min &&
+                                                              orow_last < args.T_out);
+                if (fast) {
+                    // residual rows of both chunks in flight before the accumulator reads
+                    const size_t rstep = (size_t)args.o_stride * args.ldres, ystep = (size_t)args.o_stride * args.ldy;
+                    float rv[64];
                     if (args.res) {
-                        const float* rp = args.res + (size_t)rrow * args.ldres + co;
-                        if (vec && (args.ldres & 3) == 0) {
-                            const float4 r4 = *reinterpret_cast<const float4*>(rp);
-                            o.x += r4.x; o.y += r4.y; o.z += r4.z; o.w += r4.w;
-                        } else {
-                            o.x += rp[0];
-                            if (ncol > 1) o.y += rp[1];
-                            if (ncol > 2) o.z += rp[2];
-                            if (ncol > 3) o.w += rp[3];
+                        const float* rp = args.res + (size_t)orow_p * args.ldres + co;
+#pragma unroll
+                        for (int j = 0; j < 64; j++) rv[j] = rp[j * rstep];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 64; j++) rv[j] = 0.f;
+                    }
+                    float* yp = args.y + (size_t)orow_p * args.ldy + co;
+#pragma unroll
+                    for (int cc = 0; cc < 2; cc++) {
+                        float v[32];
+                        tmem_ld32(s_tmem + (uint32_t)((2 * pp + cc) * 32), v);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            float o = v[j];
+                            if (args.res) o += rv[cc * 32 + j];
+                            o += bias_v;
+                            o *= args.alpha;
+                            yp[(cc * 32 + j) * ystep] = o;
+                            s += o;
+                            q += o * o;
                         }
                     }
-                    o.x += bias4.x; o.y += bias4.y; o.z += bias4.z; o.w += bias4.w;
-                    if (args.act == 1) {
-                        o.x = gelu_tanh(o.x); o.y = gelu_tanh(o.y); o.z = gelu_tanh(o.z); o.w = gelu_tanh(o.w);
-                    }
-                    if (args.acc_in) {
-                        const float* ap = args.acc_in + (size_t)orow * args.ldacc + co;
-                        o.x = ap[0] + o.x;
-                        if (ncol > 1) o.y = ap[1] + o.y;
-                        if (ncol > 2) o.z = ap[2] + o.z;
-                        if (ncol > 3) o.w = ap[3] + o.w;
-                    }
-                    o.x *= args.alpha; o.y *= args.alpha; o.z *= args.alpha; o.w *= args.alpha;
-                    float* yp = args.y + (size_t)orow * args.ldy + co;
-                    if (vec && (args.ldy & 3) == 0) {
-                        *reinterpret_cast<float4*>(yp) = o;
-                    } else {
-                        yp[0] = o.x;
-                        if (ncol > 1) yp[1] = o.y;
-                        if (ncol > 2) yp[2] = o.z;
-                        if (ncol > 3) yp[3] = o.w;
-                    }
-                    if (ncol < 4) { o.w = 0.f; if (ncol < 3) o.z = 0.f; if (ncol < 2) o.y = 0.f; }
-                    s4.x += o.x; s4.y += o.y; s4.z += o.z; s4.w += o.w;
-                    q4.x += o.x * o.x; q4.y += o.y * o.y; q4.z += o.z * o.z; q4.w += o.w * o.w;
-                }
-            }
-            if (want_stats) {
+                } else {
+#pragma unroll 1
+                    for (int cc = 0; cc < 2; cc++) {
+                        const int c = 2 * pp + cc;
+                        const int mc = m0 + c * 32;
+                        const int orow0 = mc * args.o_stride + args.o_off + phase * args.o_phase_step;
+                        float rv[32];
 #pragma unroll
-                for (int off = 8; off <= 16; off <<= 1) {
-                    s4.x += __shfl_xor_sync(0xffffffffu, s4.x, off);
-                    s4.y += __shfl_xor_sync(0xffffffffu, s4.y, off);
-                    s4.z += __shfl_xor_sync(0xffffffffu, s4.z, off);
-                    s4.w += __shfl_xor_sync(0xffffffffu, s4.w, off);
-                    q4.x += __shfl_xor_sync(0xffffffffu, q4.x, off);
-                    q4.y += __shfl_xor_sync(0xffffffffu, q4.y, off);
-                    q4.z += __shfl_xor_sync(0xffffffffu, q4.z, off);
-                    q4.w += __shfl_xor_sync(0xffffffffu, q4.w, off);
+                        for (int j = 0; j < 32; j++) {
+                            const int orow = orow0 + j * args.o_stride;
+                            const bool val = co_ok && mc + j < args.M && orow >= args.o_min && orow < args.T_out;
+                            rv[j] = (args.res && val) ? args.res[(size_t)(orow >> args.res_shift) * args.ldres + co]
+                                                      : 0.f;
+                        }
+                        float v[32];
+                        tmem_ld32(s_tmem + (uint32_t)(c * 32), v);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int orow = orow0 + j * args.o_stride;
+                            if (!(co_ok && mc + j < args.M && orow >= args.o_min && orow < args.T_out)) continue;
+                            float o = v[j];
+                            if (args.res) o += rv[j];
+                            o += bias_v;
+                            if (args.act == 1) o = gelu_tanh(o);
+                            if (args.acc_in) o = args.acc_in[(size_t)orow * args.ldacc + co] + o;
+                            o *= args.alpha;
+                            args.y[(size_t)orow * args.ldy + co] = o;
+                            s += o;
+                            q += o * o;
+                            // reflection pad (1, 0): the accumulator of dup_src_row also goes to
+                            // row 0, with residual / accumulator row 0
+                            if (orow == args.dup_src_row) {
+                                float o0 = v[j];
+                                if (args.res) o0 += args.res[co];
+                                o0 += bias_v;
+                                if (args.act == 1) o0 = gelu_tanh(o0);
+                                if (args.acc_in) o0 = args.acc_in[co] + o0;
+                                o0 *= args.alpha;
+                                args.y[co] = o0;
+                                s += o0;
+                                q += o0 * o0;
+                            }
+                        }
+                    }
                 }
-                if (rsub == 0) {
-                    float* rs = red + (size_t)wq * NB + c * 32 + cg * 4;
-                    float* rq = red + (size_t)(4 + wq) * NB + c * 32 + cg * 4;
-                    rs[0] = s4.x; rs[1] = s4.y; rs[2] = s4.z; rs[3] = s4.w;
-                    rq[0] = q4.x; rq[1] = q4.y; rq[2] = q4.z; rq[3] = q4.w;
-                }
-            }
-            __syncwarp();
-        }
-        if (want_stats) {
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const int part = blockIdx.z * gridDim.x + blockIdx.x;
-            for (int col = threadIdx.x - 64; col < NB; col += 128) {
-                const int co = n0 + col;
-                if (co < args.C_out) {
-                    const float s = (red[0 * NB + col] + red[1 * NB + col]) + (red[2 * NB + col] + red[3 * NB + col]);
-                    const float q = (red[4 * NB + col] + red[5 * NB + col]) + (red[6 * NB + col] + red[7 * NB + col]);
+                if (want_stats && mp < args.M && co_ok) {
+                    const int part = phase * parts_per_phase + mp / STATS_ROWS;
                     args.stats[(size_t)part * args.stats_ld + co] = s;
                     args.stats[(size_t)(args.stats_parts + part) * args.stats_ld + co] = q;
                 }
             }
+            // this warp's share of the accumulator has been read: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            // all eight epilogue warps meet here every tile, whatever happened above
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (epi_dead) break;
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        tmem_dealloc(tmem, 2 * BN);
     }
 }
 
@@ -306,21 +360,65 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int NB, bool SPLIT>
+template <int BN, bool SPLIT>
 cudaError_t set_attr() {
-    return cudaFuncSetAttribute(conv_tc_kernel<NB, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)Cfg<NB, SPLIT>::SMEM_MAX);
+    return cudaFuncSetAttribute(conv_tc_kernel<BN, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)SMEM_LIMIT);
 }
 
-template <int NB, bool SPLIT>
-cudaError_t launch_inst(const ConvOperands& ops, const ConvArgs& a, int n_phases, cudaStream_t stream) {
-    using C = Cfg<NB, SPLIT>;
-    const size_t smem = C::smem_bytes(a.h_pad);
-    if (smem > C::SMEM_MAX) return cudaErrorInvalidValue;
-    dim3 grid((a.M + BM - 1) / BM, (a.C_out + NB - 1) / NB, n_phases);
-    conv_tc_kernel<NB, SPLIT><<<grid, 192, smem, stream>>>(ops.a_hi, SPLIT ? ops.a_lo : ops.a_hi, ops.b_hi,
-                                                            SPLIT ? ops.b_lo : ops.b_hi, a);
+// SM count of the current device (cached per device).
+int sm_count() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+// Activation box rows for a BN-row tile: the tile (BN + halo rows) is loaded
+// as two boxes of this many rows (a TMA box is at most 256 rows).
+int act_box_rows(int BN, int halo) {
+    const int half = (BN + halo + 1) / 2;
+    return (half + 7) / 8 * 8;
+}
+
+template <int BN, bool SPLIT>
+cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_phases, cudaStream_t stream) {
+    using C = Cfg<BN, SPLIT>;
+    a.act_box = act_box_rows(BN, halo);
+    const int ws = C::w_stages(a.act_box);
+    if (ws < 2 || a.act_box > 256) return cudaErrorInvalidValue;
+    CUtensorMap x_hi, x_lo;
+    if (!make_tmap_k64(&x_hi, ops.act_hi, SPLIT, ops.act_cp, ops.act_rows, ops.act_cp, a.act_box) ||
+        (SPLIT && !make_tmap_k64(&x_lo, ops.act_lo, true, ops.act_cp, ops.act_rows, ops.act_cp, a.act_box)))
+        return cudaErrorInvalidValue;
+    if (!SPLIT) x_lo = x_hi;
+    const size_t smem = C::smem_bytes(a.act_box, ws);
+    const int tiles = ((a.M + BN - 1) / BN) * ((a.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS) * n_phases;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    conv_tc_kernel<BN, SPLIT><<<grid, 320, smem, stream>>>(x_hi, x_lo, ops.w_hi, SPLIT ? ops.w_lo : ops.w_hi, a,
+                                                            n_phases, ws);
     return cudaGetLastError();
+}
+
+// Largest time tile that still gives the launch most of a wave of tiles and
+// whose activation ring fits in shared memory.
+int pick_bn(int M, int C_out, int n_phases, int halo, bool split) {
+    const int ctiles = (C_out + CONV_W_ROWS - 1) / CONV_W_ROWS * n_phases;
+    const int want = (sm_count() * 2) / 3;
+    const int cands[3] = {256, 128, 64};
+    for (int i = 0; i < 3; i++) {
+        const int bn = cands[i];
+        const int box = act_box_rows(bn, halo);
+        const int ws = split ? Cfg<256, true>::w_stages(box) : Cfg<256, false>::w_stages(box);
+        if (ws < 2 || box > 256) continue;
+        if (bn == 64 || (M + bn - 1) / bn * ctiles >= want) return bn;
+    }
+    return 0;
 }
 
 }  // namespace
@@ -343,48 +441,38 @@ bool make_tmap_k64(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, u
 
 cudaError_t conv_tc_init() {
     cudaError_t e;
-    if ((e = set_attr<128, true>()) || (e = set_attr<128, false>()) || (e = set_attr<64, true>()) ||
-        (e = set_attr<64, false>()) || (e = set_attr<32, true>()) || (e = set_attr<32, false>()))
+    if ((e = set_attr<256, true>()) || (e = set_attr<256, false>()) || (e = set_attr<128, true>()) ||
+        (e = set_attr<128, false>()) || (e = set_attr<64, true>()) || (e = set_attr<64, false>()))
         return e;
     return cudaSuccess;
 }
 
-int conv_tc_ntile(int C_out) {
-    if (C_out > 64) return 128;
-    if (C_out > 32) return 64;
-    return 32;
-}
-
-int conv_tc_halo_rows(const int* tap_off, int taps) {
-    int lo = tap_off[0], hi = tap_off[0];
-    for (int k = 1; k < taps; k++) {
-        lo = tap_off[k] < lo ? tap_off[k] : lo;
-        hi = tap_off[k] > hi ? tap_off[k] : hi;
-    }
-    const int h = BM + hi - lo;
-    return (h + 7) / 8 * 8;
-}
-
 cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a_in, bool split, int n_phases,
                            cudaStream_t stream) {
-    if (a_in.taps < 1 || a_in.taps > CONV_MAX_TAPS || a_in.kblocks < 1 || a_in.M < 1) return cudaErrorInvalidValue;
+    if (a_in.taps < 1 || a_in.taps > CONV_MAX_TAPS || a_in.kblocks < 1 || a_in.M < 1 || n_phases < 1 ||
+        !ops.act_hi || (split && !ops.act_lo) || ops.act_cp != (uint64_t)a_in.kblocks * 64)
+        return cudaErrorInvalidValue;
+    if (a_in.stats && a_in.stats_parts != conv_tc_stats_parts(a_in.M, n_phases)) return cudaErrorInvalidValue;
     ConvArgs a = a_in;
-    int lo = a.tap_off[0];
-    for (int k = 1; k < a.taps; k++) lo = a.tap_off[k] < lo ? a.tap_off[k] : lo;
+    int lo = a.tap_off[0], hi = a.tap_off[0];
+    for (int k = 1; k < a.taps; k++) {
+        lo = a.tap_off[k] < lo ? a.tap_off[k] : lo;
+        hi = a.tap_off[k] > hi ? a.tap_off[k] : hi;
+    }
     a.min_off = lo;
-    a.h_pad = conv_tc_halo_rows(a.tap_off, a.taps);
-    if (a.h_pad > MAX_HPAD) return cudaErrorInvalidValue;
     // Row-shifted descriptor starts use base offset 0: the 128-byte swizzle phase
     // follows the absolute shared-memory address (checked on B200 against the
     // float64 convolution for shifts that are not multiples of 8 rows).
     a.desc_mode = 0;
-    switch (conv_tc_ntile(a.C_out)) {
-        case 128: return split ? launch_inst<128, true>(ops, a, n_phases, stream)
-                               : launch_inst<128, false>(ops, a, n_phases, stream);
-        case 64: return split ? launch_inst<64, true>(ops, a, n_phases, stream)
-                              : launch_inst<64, false>(ops, a, n_phases, stream);
-        default: return split ? launch_inst<32, true>(ops, a, n_phases, stream)
-                              : launch_inst<32, false>(ops, a, n_phases, stream);
+    const int halo = hi - lo;
+    switch (pick_bn(a.M, a.C_out, n_phases, halo, split)) {
+        case 256: return split ? launch_inst<256, true>(ops, a, halo, n_phases, stream)
+                               : launch_inst<256, false>(ops, a, halo, n_phases, stream);
+        case 128: return split ? launch_inst<128, true>(ops, a, halo, n_phases, stream)
+                               : launch_inst<128, false>(ops, a, halo, n_phases, stream);
+        case 64: return split ? launch_inst<64, true>(ops, a, halo, n_phases, stream)
+                              : launch_inst<64, false>(ops, a, halo, n_phases, stream);
+        default: return cudaErrorInvalidValue;
     }
 }
 

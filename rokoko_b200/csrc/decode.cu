@@ -30,7 +30,7 @@ namespace rk {
 
 
 
-int stats_parts_for(const ConvCall& cc) { return ((cc.M + 127) / 128) * cc.w->phases; }
+int stats_parts_for(const ConvCall& cc) { return conv_tc_stats_parts(cc.M, cc.w->phases); }
 
 void conv(Run& r, const ConvCall& cc) {
     if (!r.ok()) return;
@@ -42,15 +42,12 @@ void conv(Run& r, const ConvCall& cc) {
     }
     int toff[CONV_MAX_TAPS];
     for (int k = 0; k < w.taps; k++) toff[k] = w.phases > 1 ? -k : (w.stride > 1 ? k : k * cc.dil - cc.pad);
-    const int hrows = conv_tc_halo_rows(toff, w.taps);
-    if (!make_tmap_k64(&ops.a_hi, cc.op->hi, cc.split, w.Cp, cc.rows_in, w.Cp, hrows) ||
-        (cc.split && !make_tmap_k64(&ops.a_lo, cc.op->lo, true, w.Cp, cc.rows_in, w.Cp, hrows))) {
-        r.status = fail(RK_ERR_INIT, "activation tensor map");
-        return;
-    }
-    if (!cc.split) ops.a_lo = ops.a_hi;
-    ops.b_hi = w.tm_hi;
-    ops.b_lo = w.tm_lo;
+    ops.act_hi = cc.op->hi;
+    ops.act_lo = cc.split ? cc.op->lo : nullptr;
+    ops.act_rows = (uint64_t)cc.rows_in;
+    ops.act_cp = (uint64_t)w.Cp;
+    ops.w_hi = w.tm_hi;
+    ops.w_lo = w.tm_lo;
     ConvArgs a{};
     a.M = cc.M;
     a.C_out = w.C_out;
@@ -198,7 +195,7 @@ void resblock1(Run& r, Lane& ln, const ResBlock1W& rb, const float* x0, const fl
     const int dil[3] = {1, 3, 5};
     const float* x = x0;
     const float* sx = sx0;
-    const int parts = (T + 127) / 128;
+    const int parts = conv_tc_stats_parts(T, 1);
     int px = parts0;
     float* nxt[2] = {ln.xa, ln.xb};
     float* nst[2] = {ln.stats_b, ln.stats_c};
@@ -246,7 +243,7 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
     const size_t L2 = 2 * (size_t)L, T1 = 20 * (size_t)L, T2 = 120 * (size_t)L + 1, TA = 600 * (size_t)L;
     const size_t gen = std::max(T1 * 256, T2 * 128);
     const size_t dec = L2 * 1024;
-    const size_t parts = (T2 + 127) / 128 + 16;
+    const size_t parts = (T2 + STATS_ROWS - 1) / STATS_ROWS + 16;
     const size_t stats = 2 * parts * 1090;
     const size_t plane = std::max({T2 * 128, T1 * 256, L2 * 1152, L2 * 512}) * 2;
     struct Req { float** p; size_t n; };
@@ -345,7 +342,7 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     r.check_launch("f0n_down");
     concat_cols(w.cat514, 514, 0, L, w.asr, 512, 512, nullptr, 0, 0, w.f0d, w.nd, r.st);
     r.check_launch("concat514");
-    col_stats(w.cat514, 514, 0, 514, L, 128, w.stats_cat514, r.st);
+    col_stats(w.cat514, 514, 0, 514, L, STATS_ROWS, w.stats_cat514, r.st);
     r.check_launch("col_stats");
     {  // asr_res: Conv1d 512 -> 64 (K1), FP32 semantics in both precisions
         pack(r, w.asr, 512, L, 512, w.op_b, d.asr_res.Cp, true);
@@ -354,11 +351,11 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
         ca.y = w.asr_res; ca.ldy = 64;
         conv(r, ca);
     }
-    const int parts_L = (L + 127) / 128;
+    const int parts_L = conv_tc_stats_parts(L, 1);
     for (int i = 0; i < 4; i++) {  // side channels of the decode-block inputs: [x | asr_res | F0d | Nd]
         concat_cols(w.in1090[i], 1090, 1024, L, w.asr_res, 64, 64, nullptr, 0, 0, w.f0d, w.nd, r.st);
         r.check_launch("concat_side");
-        col_stats(w.in1090[i], 1090, 1024, 66, L, 128, w.stats_in[i], r.st);
+        col_stats(w.in1090[i], 1090, 1024, 66, L, STATS_ROWS, w.stats_in[i], r.st);
         r.check_launch("col_stats");
     }
     resblk1d(r, d.encode, w.cat514, 514, w.stats_cat514, parts_L, 514, L, w.in1090[0], 1090, w.stats_in[0], 1090,

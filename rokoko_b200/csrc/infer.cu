@@ -100,8 +100,8 @@ rk_status ensure_front_frames(rk_ctx* c, int L_b) {
     std::vector<Req> reqs = {
         {(void**)&f.ig, rows * 2048 * 4}, {(void**)&f.en, L * 640 * 4}, {(void**)&f.shared, L * 512 * 4},
         {(void**)&f.x1, L * 512 * 4}, {(void**)&f.x2, 2 * L * 256 * 4}, {(void**)&f.x3, 2 * L * 256 * 4},
-        {(void**)&f.stats, 2 * ((L + 127) / 128 + 8) * 512 * 4},
-        {(void**)&f.stats2, 2 * ((L + 127) / 128 + 8) * 512 * 4},
+        {(void**)&f.stats, 2 * ((2 * L + STATS_ROWS - 1) / STATS_ROWS + 8) * 512 * 4},
+        {(void**)&f.stats2, 2 * ((2 * L + STATS_ROWS - 1) / STATS_ROWS + 8) * 512 * 4},
     };
     const size_t plane = al(std::max((size_t)c->max_tokens * 2048, L * 640) * 2);
     char* rest = alloc_group(reqs, 2 * plane, f.frame_allocs);
@@ -191,19 +191,19 @@ rk_status enqueue_predict(rk_ctx* c, int T, int L_b) {
     lstm(r, F.shared, f.op, L_b, f.shared);
     record(r, "shared", f.shared, (size_t)L_b * 512);
     record(r, "asr_aligned", w.asr, (size_t)L_b * 512);
-    const int parts = (L_b + 127) / 128;
-    col_stats(f.shared, 512, 0, 512, L_b, 128, f.stats, r.st);
+    const int parts = conv_tc_stats_parts(L_b, 1);
+    col_stats(f.shared, 512, 0, 512, L_b, STATS_ROWS, f.stats, r.st);
     r.check_launch("col_stats");
     for (int chain = 0; chain < 2 && r.ok(); chain++) {
         const ResBlk1dW* b = chain == 0 ? F.f0 : F.nn;
         resblk1d(r, b[0], f.shared, 512, f.stats, parts, 512, L_b, f.x1, 512, f.stats2, 512, F.fc);
         resblk1d(r, b[1], f.x1, 512, f.stats2, parts, 512, L_b, f.x2, 256, f.stats, 256, F.fc);
-        resblk1d(r, b[2], f.x2, 256, f.stats, (2 * L_b + 127) / 128, 256, 2 * L_b, f.x3, 256, nullptr, 0, F.fc);
+        resblk1d(r, b[2], f.x2, 256, f.stats, conv_tc_stats_parts(2 * L_b, 1), 256, 2 * L_b, f.x3, 256, nullptr, 0, F.fc);
         rowdot(f.x3, 2 * L_b, 256, chain == 0 ? F.f0_proj_w : F.n_proj_w, chain == 0 ? F.f0_proj_b : F.n_proj_b,
                chain == 0 ? w.f0 : w.n, r.st);
         r.check_launch("rowdot");
         if (chain == 0) {  // the N chain reuses the statistics buffer of `shared`
-            col_stats(f.shared, 512, 0, 512, L_b, 128, f.stats, r.st);
+            col_stats(f.shared, 512, 0, 512, L_b, STATS_ROWS, f.stats, r.st);
             r.check_launch("col_stats");
         }
     }

@@ -5,7 +5,7 @@
 // Workspace layout (256-byte aligned slabs):
 //   [0, 256)          device error word (uint32) + padding
 //   activation planes  rows x Cp 16-bit, hi then lo (split)
-//   weight planes      C_out x taps x Cp 16-bit, hi then lo (split)
+//   weight planes      C_out (padded to a multiple of 128) x taps x Cp 16-bit, hi then lo (split)
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -43,7 +43,7 @@ bool plan_conv(int C_in, int C_out, int T_in, int K, int stride, int pad, int di
     if (p.taps > rk::CONV_MAX_TAPS) return false;
     const int planes = precision == RK_PRECISION_FP32 ? 2 : 1;
     p.act_plane = al256((size_t)p.rows * p.Cp * 2);
-    p.w_plane = al256((size_t)C_out * p.taps * p.Cp * 2);
+    p.w_plane = al256((size_t)rk::conv_tc_weight_rows(C_out) * p.taps * p.Cp * 2);
     p.total = 256 + planes * (p.act_plane + p.w_plane);
     return true;
 }
@@ -92,16 +92,18 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
         if (rk::conv_tc_init() != cudaSuccess) return rk::fail_cuda(RK_ERR_INIT, "conv_tc_init");
         init_dev = dev;
     }
+    // weight rows beyond C_out (padding up to the 128-row tile) only feed
+    // accumulator rows the epilogue never stores
     rk::ConvOperands ops;
-    const int nt = rk::conv_tc_ntile(C_out);
-    const int hrows = rk::conv_tc_halo_rows(p.tap_off, p.taps);
-    if (!rk::make_tmap_k64(&ops.a_hi, a_hi, split, p.Cp, p.rows, p.Cp, hrows) ||
-        !rk::make_tmap_k64(&ops.b_hi, w_hi, split, (uint64_t)p.taps * p.Cp, C_out, (uint64_t)p.taps * p.Cp, nt) ||
-        (split && (!rk::make_tmap_k64(&ops.a_lo, a_lo, true, p.Cp, p.rows, p.Cp, hrows) ||
-                   !rk::make_tmap_k64(&ops.b_lo, w_lo, true, (uint64_t)p.taps * p.Cp, C_out,
-                                      (uint64_t)p.taps * p.Cp, nt))))
+    ops.act_hi = a_hi;
+    ops.act_lo = split ? a_lo : nullptr;
+    ops.act_rows = (uint64_t)p.rows;
+    ops.act_cp = (uint64_t)p.Cp;
+    const uint64_t wcols = (uint64_t)p.taps * p.Cp, wrows = (uint64_t)rk::conv_tc_weight_rows(C_out);
+    if (!rk::make_tmap_k64(&ops.w_hi, w_hi, split, wcols, wrows, wcols, rk::CONV_W_ROWS) ||
+        (split && !rk::make_tmap_k64(&ops.w_lo, w_lo, true, wcols, wrows, wcols, rk::CONV_W_ROWS)))
         return rk::fail(RK_ERR_INIT, "rk_conv1d_fprop: tensor map encoding failed");
-    if (!split) { ops.a_lo = ops.a_hi; ops.b_lo = ops.b_hi; }
+    if (!split) ops.w_lo = ops.w_hi;
 
     rk::ConvArgs a{};
     a.M = p.T_out; a.C_out = C_out; a.kblocks = p.Cp / 64; a.taps = p.taps;

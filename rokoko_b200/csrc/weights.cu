@@ -161,16 +161,19 @@ struct Loader {
     }
 
     void make_maps(ConvW& cw) {
-        const int nt = conv_tc_ntile(cw.C_out);
-        const uint64_t cols = (uint64_t)cw.taps * cw.Cp, rows = (uint64_t)cw.phases * cw.C_out;
-        if (!make_tmap_k64(&cw.tm_hi, cw.hi, split, cols, rows, cols, nt) ||
-            (split && !make_tmap_k64(&cw.tm_lo, cw.lo, true, cols, rows, cols, nt)))
+        const uint64_t cols = (uint64_t)cw.taps * cw.Cp;
+        const uint64_t rows = (uint64_t)conv_tc_weight_rows(cw.phases * cw.C_out);
+        if (!make_tmap_k64(&cw.tm_hi, cw.hi, split, cols, rows, cols, CONV_W_ROWS) ||
+            (split && !make_tmap_k64(&cw.tm_lo, cw.lo, true, cols, rows, cols, CONV_W_ROWS)))
             throw WeightError("tensor map encoding failed (weights)");
         if (!split) cw.tm_lo = cw.tm_hi;
     }
 
     // planes[row][col] <- host floats, converted to bf16 hi/lo or fp16.
-    void upload_planes(ConvW& cw, const std::vector<float>& p) {
+    void upload_planes(ConvW& cw, const std::vector<float>& p_in) {
+        // rows padded with zeros to a multiple of the kernel's 128-row weight tile
+        std::vector<float> p(p_in);
+        p.resize((size_t)conv_tc_weight_rows(cw.phases * cw.C_out) * cw.taps * cw.Cp, 0.f);
         const size_t n = p.size();
         if (split) {
             std::vector<__nv_bfloat16> h(n), l(n);

@@ -22,6 +22,9 @@ CASES = [
     (512, 64, 400, 1, 1, 0, 1, False),
     (22, 128, 333, 1, 1, 0, 1, False),
     (768, 2048, 66, 1, 1, 0, 1, False),
+    # more tiles than SMs: each persistent CTA runs several tiles through both accumulators
+    (128, 128, 48001, 7, 1, 9, 3, True),
+    (128, 128, 100000, 3, 1, 1, 1, False),
 ]
 
 

@@ -58,7 +58,19 @@ __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, in
     const int c = blockIdx.x * 32 + cx;
     double s = 0.0, q = 0.0;
     if (c < C) {
-        for (int p = py; p < parts; p += 32) {
+        // four parts per step, loads issued together (fixed summation order: p ascending per thread)
+        int p = py;
+        for (; p + 96 < parts; p += 128) {
+            const float s0 = stats[(size_t)p * ld + col0 + c], s1 = stats[(size_t)(p + 32) * ld + col0 + c];
+            const float s2 = stats[(size_t)(p + 64) * ld + col0 + c], s3 = stats[(size_t)(p + 96) * ld + col0 + c];
+            const float q0 = stats[(size_t)(parts + p) * ld + col0 + c];
+            const float q1 = stats[(size_t)(parts + p + 32) * ld + col0 + c];
+            const float q2 = stats[(size_t)(parts + p + 64) * ld + col0 + c];
+            const float q3 = stats[(size_t)(parts + p + 96) * ld + col0 + c];
+            s += s0; s += s1; s += s2; s += s3;
+            q += q0; q += q1; q += q2; q += q3;
+        }
+        for (; p < parts; p += 32) {
             s += stats[(size_t)p * ld + col0 + c];
             q += stats[(size_t)(parts + p) * ld + col0 + c];
         }

@@ -66,6 +66,45 @@ __global__ void pack_act_kernel(PackArgs a) {
     }
 }
 
+// Fast path: plain rows (no super-row gather), C a multiple of 8.  One thread
+// = 8 channels of one row: two float4 loads, one 16-byte store per plane.
+template <bool SPLIT>
+__global__ void pack_act_vec_kernel(PackArgs a) {
+    const int groups = a.Cp >> 3, cgroups = a.C >> 3;
+    const long total = (long)a.rows_dst * groups;
+    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int q = (int)(idx / groups);
+        const int g = (int)(idx - (long)q * groups);
+        float v[8];
+        if (g < cgroups && q < a.rows_src) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (long)q * a.ldx + g * 8);
+            const float4 p0 = src[0], p1 = src[1];
+            v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+            v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = act_transform(v[j], g * 8 + j, a);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.0f;
+        }
+        if (SPLIT) {
+            __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                h[j] = __float2bfloat16_rn(v[j]);
+                l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+            }
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
+            reinterpret_cast<uint4*>(a.lo)[idx] = *reinterpret_cast<uint4*>(l);
+        } else {
+            __align__(16) __half h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
 template <bool SPLIT>
 __global__ void pack_w_kernel(const float* w, int C_out, int K, int C_in, int stride, int taps, int Cp, void* hi,
                               void* lo) {
@@ -142,8 +181,15 @@ cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
     if ((a.Cp & 63) || a.sr_stride < 1) return cudaErrorInvalidValue;
     const long total = (long)a.rows_dst * (a.Cp >> 3);
     if (total == 0) return cudaSuccess;
-    if (split) pack_act_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
-    else pack_act_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+    const bool vec = a.sr_stride == 1 && a.sr_pad == 0 && (a.C & 7) == 0 && (a.ldx & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+    if (vec) {
+        if (split) pack_act_vec_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
+        else pack_act_vec_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+    } else {
+        if (split) pack_act_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
+        else pack_act_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+    }
     return cudaGetLastError();
 }
 

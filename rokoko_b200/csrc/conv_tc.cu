@@ -6,7 +6,7 @@
 // ConvTranspose1d (src/rokoko.cpp:308-329, src/kernels.cu:1141-1173).
 //
 // Orientation: the weights are the MMA's M = 128 side (output channels) and
-// the activations the N side (BN = 64, 128 or 256 time rows), so one weight
+// the activations the N side (BN = 64, 128, 192 or 256 time rows), so one weight
 // tile streamed from L2 feeds BN rows of output; at BN = 256 the tensor pipe
 // runs near its peak with a two-deep weight ring (measured on B200: the same
 // stream at N = 128 saturates the L2 -> SMEM path first).
@@ -47,6 +47,7 @@ constexpr int BK = 64;
 constexpr int X_STAGES = 2;
 constexpr int MAX_W_STAGES = 8;
 constexpr size_t SMEM_LIMIT = 227 * 1024 - 1024;  // dynamic bytes; leaves room for the static barriers
+constexpr int MAX_K_SPLIT = 8;
 
 template <int BN, bool SPLIT>
 struct Cfg {
@@ -61,6 +62,9 @@ struct Cfg {
         return n > MAX_W_STAGES ? MAX_W_STAGES : n;
     }
     static size_t smem_bytes(int box, int ws) { return fixed_bytes(box) + (size_t)ws * W_STAGE; }
+    // TMEM: two accumulators of BN columns, ACC_STRIDE apart; the allocation is a power of two
+    static constexpr uint32_t TMEM_ALLOC = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
+    static constexpr uint32_t ACC_STRIDE = TMEM_ALLOC / 2;
 };
 
 // gelu_new: 0.5 v (1 + tanh(0.7978845608 (v + 0.044715 v^3)))
@@ -70,10 +74,13 @@ __device__ __forceinline__ float gelu_tanh(float v) {
 }
 
 struct Tiles {
-    int tiles_t, tiles_c, n_tiles;
-    __device__ void decode(int t, int& t_tile, int& c_tile, int& phase) const {
-        phase = t / (tiles_t * tiles_c);
-        const int rem = t - phase * tiles_t * tiles_c;
+    int tiles_t, tiles_c, n_phases, n_tiles;
+    __device__ void decode(int t, int& t_tile, int& c_tile, int& phase, int& ks) const {
+        const int per = tiles_t * tiles_c * n_phases;
+        ks = t / per;
+        int rem = t - ks * per;
+        phase = rem / (tiles_t * tiles_c);
+        rem -= phase * tiles_t * tiles_c;
         c_tile = rem / tiles_t;
         t_tile = rem - c_tile * tiles_t;
     }
@@ -100,10 +107,12 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t* x_buf = smem;                                       // [stage][plane][2*box rows][128 B]
     uint8_t* w_buf = smem + (size_t)X_STAGES * x_stage;          // [stage][plane][128 rows][128 B]
     const int KB = args.kblocks, TAPS = args.taps;
+    const int S = args.k_split > 1 ? args.k_split : 1;
     Tiles g;
     g.tiles_t = (args.M + BN - 1) / BN;
     g.tiles_c = (args.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS;
-    g.n_tiles = g.tiles_t * g.tiles_c * n_phases;
+    g.n_phases = n_phases;
+    g.n_tiles = g.tiles_t * g.tiles_c * n_phases * S;
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < X_STAGES; s++) { mbar_init(&x_full[s], 1); mbar_init(&x_empty[s], 1); }
@@ -117,7 +126,7 @@ __global__ void __launch_bounds__(320, 1)
         if (SPLIT) { tma_prefetch_desc(&tmX_lo); tma_prefetch_desc(&tmW_lo); }
     }
     if (warp == 1) {
-        tmem_alloc(&tmem_base_sh, 2 * BN);
+        tmem_alloc(&tmem_base_sh, C::TMEM_ALLOC);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -131,11 +140,12 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t xi = 0, wi = 0;
             bool alive = true;
             for (int t = blockIdx.x; t < g.n_tiles && alive; t += gridDim.x) {
-                int t_tile, c_tile, phase;
-                g.decode(t, t_tile, c_tile, phase);
+                int t_tile, c_tile, phase, ks;
+                g.decode(t, t_tile, c_tile, phase, ks);
                 const int wrow = phase * args.b_phase_rows + c_tile * CONV_W_ROWS;
                 const int xrow = t_tile * BN + args.a_off + args.min_off;
-                for (int kb = 0; kb < KB && alive; kb++, xi++) {
+                const int kb1 = (ks + 1) * KB / S;
+                for (int kb = ks * KB / S; kb < kb1 && alive; kb++, xi++) {
                     const uint32_t sx = xi % X_STAGES, rx = xi / X_STAGES;
                     if (!mbar_wait(&x_empty[sx], (rx & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) { alive = false; break; }
                     uint8_t* xb = x_buf + (size_t)sx * x_stage;
@@ -173,11 +183,14 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t xi = 0, wi = 0, tl = 0;
             bool alive = true;
             for (int t = blockIdx.x; t < g.n_tiles && alive; t += gridDim.x, tl++) {
+                int t_tile, c_tile, phase, ks;
+                g.decode(t, t_tile, c_tile, phase, ks);
+                const int kb0 = ks * KB / S, kb1 = (ks + 1) * KB / S;
                 const uint32_t acc = tl & 1u, ru = tl >> 1;
                 if (!mbar_wait(&acc_empty[acc], (ru & 1u) ^ 1u, args.err, RK_DEV_TIMEOUT_EMPTY)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + acc * BN;
-                for (int kb = 0; kb < KB && alive; kb++, xi++) {
+                const uint32_t d_tmem = tmem + acc * C::ACC_STRIDE;
+                for (int kb = kb0; kb < kb1 && alive; kb++, xi++) {
                     const uint32_t sx = xi % X_STAGES, rx = xi / X_STAGES;
                     if (!mbar_wait(&x_full[sx], rx & 1u, args.err, RK_DEV_TIMEOUT_FULL)) { alive = false; break; }
                     tc_fence_after();
@@ -195,7 +208,7 @@ __global__ void __launch_bounds__(320, 1)
                         for (int kk = 0; kk < BK / 16; kk++) {
                             const uint64_t dwh = sw128_kmajor_desc(w_hi + kk * 32, 0);
                             const uint64_t dxh = sw128_kmajor_desc(x_hi + shift + kk * 32, args.desc_mode);
-                            umma_f16(d_tmem, dwh, dxh, idesc, (kb > 0 || tap > 0 || kk > 0) ? 1u : 0u);
+                            umma_f16(d_tmem, dwh, dxh, idesc, (kb > kb0 || tap > 0 || kk > 0) ? 1u : 0u);
                             if (SPLIT) {
                                 umma_f16(d_tmem, dwh, sw128_kmajor_desc(x_lo + shift + kk * 32, args.desc_mode),
                                          idesc, 1u);
@@ -223,8 +236,8 @@ __global__ void __launch_bounds__(320, 1)
         const int parts_per_phase = (args.M + STATS_ROWS - 1) / STATS_ROWS;
         uint32_t tl = 0;
         for (int t = blockIdx.x; t < g.n_tiles; t += gridDim.x, tl++) {
-            int t_tile, c_tile, phase;
-            g.decode(t, t_tile, c_tile, phase);
+            int t_tile, c_tile, phase, ks;
+            g.decode(t, t_tile, c_tile, phase, ks);
             const int m0 = t_tile * BN;
             const int co = c_tile * CONV_W_ROWS + wq * 32 + lane;
             const bool co_ok = co < args.C_out;
@@ -233,13 +246,26 @@ __global__ void __launch_bounds__(320, 1)
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], ru & 1u, args.err, RK_DEV_TIMEOUT_ACC));
             tc_fence_after();
             if (!ok && lane == 0) epi_dead = 1;
-            const uint32_t s_tmem = tmem + acc * BN + ((uint32_t)(wq * 32) << 16);
+            const uint32_t s_tmem = tmem + acc * C::ACC_STRIDE + ((uint32_t)(wq * 32) << 16);
             // Common case, branch-free so the 32 rows of a chunk interleave: plain
             // residual (no row shift), no activation, no accumulator input, no
             // duplicated row, and every row of the chunk inside the output.
             const bool fast_conv = co_ok && !args.act && !args.acc_in && args.res_shift == 0 && args.dup_src_row < 0;
+            if (args.part_out) {
+                // split-K: raw accumulators of this reduction slice, rows by m
+                float* po = args.part_out + ((size_t)(ks * n_phases + phase) * args.M) * args.C_out + co;
 #pragma unroll 1
-            for (int pp = half; pp < (ok ? BN / 64 : 0); pp += 2) {
+                for (int c = half * 2; c < (ok ? BN / 32 : 0); c += (c & 1) ? 3 : 1) {
+                    float v[32];
+                    tmem_ld32(s_tmem + (uint32_t)(c * 32), v);
+                    const int mc = m0 + c * 32;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (mc + j < args.M && co_ok) po[(size_t)(mc + j) * args.C_out] = v[j];
+                }
+            }
+#pragma unroll 1
+            for (int pp = half; pp < ((ok && !args.part_out) ? BN / 64 : 0); pp += 2) {
                 float s = 0.f, q = 0.f;
                 const int mp = m0 + pp * 64;
                 const int orow_p = mp * args.o_stride + args.o_off + phase * args.o_phase_step;
@@ -340,7 +366,78 @@ __global__ void __launch_bounds__(320, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        tmem_dealloc(tmem, C::TMEM_ALLOC);
+    }
+}
+
+// Split-K second stage: one block per (128 channels, 64-row part); thread
+// (x, y) owns channel x and rows y*8 .. y*8+7 of the part.  Sums the k_split
+// raw accumulators in slice order, applies the same epilogue as the conv kernel
+// (residual, bias, activation, accumulator input, scale, reflection-pad
+// duplicate) and writes the part's statistics, combined over y in a fixed order.
+__global__ void __launch_bounds__(1024) splitk_reduce_kernel(const __grid_constant__ ConvArgs a, int n_phases) {
+    __shared__ float red_s[8][128], red_q[8][128];
+    const int cx = threadIdx.x, ry = threadIdx.y;
+    const int co = blockIdx.x * 128 + cx;
+    const int ppp = (a.M + STATS_ROWS - 1) / STATS_ROWS;
+    const int phase = blockIdx.y / ppp, p = blockIdx.y - phase * ppp;
+    const bool co_ok = co < a.C_out;
+    const size_t slice = (size_t)n_phases * a.M * a.C_out;
+    const float bias_v = (a.bias && co_ok) ? a.bias[co] : 0.0f;
+    float s = 0.f, q = 0.f;
+    const int m0 = p * STATS_ROWS + ry * 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int m = m0 + i;
+        v[i] = 0.f;
+        if (co_ok && m < a.M) {
+            // every slice's load in flight before the ordered sum
+            const float* src = a.part_out + ((size_t)phase * a.M + m) * a.C_out + co;
+            float pv[MAX_K_SPLIT];
+#pragma unroll
+            for (int k = 0; k < MAX_K_SPLIT; k++) pv[k] = k < a.k_split ? src[k * slice] : 0.f;
+            float acc = pv[0];
+#pragma unroll
+            for (int k = 1; k < MAX_K_SPLIT; k++)
+                if (k < a.k_split) acc += pv[k];
+            v[i] = acc;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int m = m0 + i;
+        const int orow = m * a.o_stride + a.o_off + phase * a.o_phase_step;
+        if (!co_ok || m >= a.M || orow < a.o_min || orow >= a.T_out) continue;
+        for (int pass = 0; pass < 2; pass++) {
+            int orw = orow, rrow = orow >> a.res_shift;
+            if (pass == 1) {
+                if (orow != a.dup_src_row) break;
+                orw = 0;
+                rrow = 0;
+            }
+            float o = v[i];
+            if (a.res) o += a.res[(size_t)rrow * a.ldres + co];
+            o += bias_v;
+            if (a.act == 1) o = gelu_tanh(o);
+            if (a.acc_in) o = a.acc_in[(size_t)orw * a.ldacc + co] + o;
+            o *= a.alpha;
+            a.y[(size_t)orw * a.ldy + co] = o;
+            s += o;
+            q += o * o;
+        }
+    }
+    if (!a.stats) return;
+    red_s[ry][cx] = s;
+    red_q[ry][cx] = q;
+    __syncthreads();
+    if (ry == 0 && co_ok) {
+        float ts = 0.f, tq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) { ts += red_s[k][cx]; tq += red_q[k][cx]; }
+        const int part = phase * ppp + p;
+        a.stats[(size_t)part * a.stats_ld + co] = ts;
+        a.stats[(size_t)(a.stats_parts + part) * a.stats_ld + co] = tq;
     }
 }
 
@@ -387,7 +484,8 @@ int act_box_rows(int BN, int halo) {
 }
 
 template <int BN, bool SPLIT>
-cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_phases, cudaStream_t stream) {
+cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_phases, cudaStream_t stream,
+                        int* kernels) {
     using C = Cfg<BN, SPLIT>;
     a.act_box = act_box_rows(BN, halo);
     const int ws = C::w_stages(a.act_box);
@@ -399,26 +497,64 @@ cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_pha
     if (!SPLIT) x_lo = x_hi;
     const size_t smem = C::smem_bytes(a.act_box, ws);
     const int tiles = ((a.M + BN - 1) / BN) * ((a.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS) * n_phases;
-    const int grid = tiles < sm_count() ? tiles : sm_count();
+    const int ks = a.k_split;
+    a.part_out = ks > 1 ? ops.scratch : nullptr;
+    const int work = tiles * ks;
+    const int grid = work < sm_count() ? work : sm_count();
     conv_tc_kernel<BN, SPLIT><<<grid, 320, smem, stream>>>(x_hi, x_lo, ops.w_hi, SPLIT ? ops.w_lo : ops.w_hi, a,
                                                             n_phases, ws);
+    cudaError_t e = cudaGetLastError();
+    if (kernels) *kernels = ks > 1 ? 2 : 1;
+    if (e != cudaSuccess || ks == 1) return e;
+    dim3 rg((a.C_out + 127) / 128, conv_tc_stats_parts(a.M, n_phases));
+    splitk_reduce_kernel<<<rg, dim3(128, 8), 0, stream>>>(a, n_phases);
     return cudaGetLastError();
 }
 
-// Largest time tile that still gives the launch most of a wave of tiles and
-// whose activation ring fits in shared memory.
-int pick_bn(int M, int C_out, int n_phases, int halo, bool split) {
-    const int ctiles = (C_out + CONV_W_ROWS - 1) / CONV_W_ROWS * n_phases;
-    const int want = (sm_count() * 2) / 3;
-    const int cands[3] = {256, 128, 64};
-    for (int i = 0; i < 3; i++) {
+// Time tile BN and split-K factor for a launch.  Estimated time = waves of
+// work units x time of one unit, where a unit is one (tile, reduction slice)
+// and its time is its MMA work over the tile's sustained tensor rate (a weight
+// tile streamed from L2 feeds BN rows: measured on B200 about full rate at
+// BN = 256, 70 % at 128, 40 % at 64), plus the split-K second pass (partials
+// written and read once at about 4 TB/s).  Only BN whose activation ring fits
+// in shared memory are considered.
+void pick_tiling(const ConvArgs& a, int n_phases, int halo, bool split, const ConvOperands& ops, int* bn_out,
+                 int* ks_out) {
+    const int ctiles = (a.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS * n_phases;
+    const int sms = sm_count();
+    const int cands[4] = {256, 192, 128, 64};
+    const double eff[4] = {1.0, 0.9, 0.7, 0.4};
+    // rows x (64-channel block) x tap per us at full tensor rate: 12 (split) or 4
+    // MMAs of 128 x 256 x 16 per 256 rows, ~128 clocks each at ~1.9 GHz
+    const double tc_rows_per_us = split ? 316.0 : 948.0;
+    const size_t slice_bytes = (size_t)n_phases * a.M * a.C_out * sizeof(float);
+    double best = 1e30;
+    *bn_out = 0;
+    *ks_out = 1;
+    for (int i = 0; i < 4; i++) {
         const int bn = cands[i];
         const int box = act_box_rows(bn, halo);
         const int ws = split ? Cfg<256, true>::w_stages(box) : Cfg<256, false>::w_stages(box);
         if (ws < 2 || box > 256) continue;
-        if (bn == 64 || (M + bn - 1) / bn * ctiles >= want) return bn;
+        const int tiles = (a.M + bn - 1) / bn * ctiles;
+        int kmax = 1;
+        if (ops.scratch && a.kblocks >= 4) {
+            kmax = a.kblocks / 2 < MAX_K_SPLIT ? a.kblocks / 2 : MAX_K_SPLIT;
+            while (kmax > 1 && (size_t)kmax * slice_bytes > ops.scratch_bytes) kmax--;
+        }
+        for (int ks = 1; ks <= kmax; ks++) {
+            const int units = tiles * ks;
+            const int waves = (units + sms - 1) / sms;
+            const double unit_us = (double)bn * a.taps * ((a.kblocks + ks - 1) / ks) / (tc_rows_per_us * eff[i]);
+            double t = waves * unit_us;
+            if (ks > 1) t += 2.0 * ks * slice_bytes / 4.0e6 + 3.0;  // second pass + its launch
+            if (t < best * 0.97) {
+                best = t;
+                *bn_out = bn;
+                *ks_out = ks;
+            }
+        }
     }
-    return 0;
 }
 
 }  // namespace
@@ -441,19 +577,23 @@ bool make_tmap_k64(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, u
 
 cudaError_t conv_tc_init() {
     cudaError_t e;
-    if ((e = set_attr<256, true>()) || (e = set_attr<256, false>()) || (e = set_attr<128, true>()) ||
-        (e = set_attr<128, false>()) || (e = set_attr<64, true>()) || (e = set_attr<64, false>()))
+    if ((e = set_attr<256, true>()) || (e = set_attr<256, false>()) || (e = set_attr<192, true>()) ||
+        (e = set_attr<192, false>()) || (e = set_attr<128, true>()) || (e = set_attr<128, false>()) ||
+        (e = set_attr<64, true>()) || (e = set_attr<64, false>()))
         return e;
     return cudaSuccess;
 }
 
 cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a_in, bool split, int n_phases,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int* kernels) {
+    if (kernels) *kernels = 0;
     if (a_in.taps < 1 || a_in.taps > CONV_MAX_TAPS || a_in.kblocks < 1 || a_in.M < 1 || n_phases < 1 ||
         !ops.act_hi || (split && !ops.act_lo) || ops.act_cp != (uint64_t)a_in.kblocks * 64)
         return cudaErrorInvalidValue;
     if (a_in.stats && a_in.stats_parts != conv_tc_stats_parts(a_in.M, n_phases)) return cudaErrorInvalidValue;
     ConvArgs a = a_in;
+    a.k_split = 1;
+    a.part_out = nullptr;
     int lo = a.tap_off[0], hi = a.tap_off[0];
     for (int k = 1; k < a.taps; k++) {
         lo = a.tap_off[k] < lo ? a.tap_off[k] : lo;
@@ -465,13 +605,17 @@ cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a_in, bool s
     // float64 convolution for shifts that are not multiples of 8 rows).
     a.desc_mode = 0;
     const int halo = hi - lo;
-    switch (pick_bn(a.M, a.C_out, n_phases, halo, split)) {
-        case 256: return split ? launch_inst<256, true>(ops, a, halo, n_phases, stream)
-                               : launch_inst<256, false>(ops, a, halo, n_phases, stream);
-        case 128: return split ? launch_inst<128, true>(ops, a, halo, n_phases, stream)
-                               : launch_inst<128, false>(ops, a, halo, n_phases, stream);
-        case 64: return split ? launch_inst<64, true>(ops, a, halo, n_phases, stream)
-                              : launch_inst<64, false>(ops, a, halo, n_phases, stream);
+    int bn = 0;
+    pick_tiling(a, n_phases, halo, split, ops, &bn, &a.k_split);
+    switch (bn) {
+        case 256: return split ? launch_inst<256, true>(ops, a, halo, n_phases, stream, kernels)
+                               : launch_inst<256, false>(ops, a, halo, n_phases, stream, kernels);
+        case 192: return split ? launch_inst<192, true>(ops, a, halo, n_phases, stream, kernels)
+                               : launch_inst<192, false>(ops, a, halo, n_phases, stream, kernels);
+        case 128: return split ? launch_inst<128, true>(ops, a, halo, n_phases, stream, kernels)
+                               : launch_inst<128, false>(ops, a, halo, n_phases, stream, kernels);
+        case 64: return split ? launch_inst<64, true>(ops, a, halo, n_phases, stream, kernels)
+                              : launch_inst<64, false>(ops, a, halo, n_phases, stream, kernels);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -6,7 +6,7 @@
 //   Linear / 1x1 conv                       K = 1
 // GEMM view (transposed, so that the wide dimension feeds the N side of the
 // MMA): D[c_out][m] = sum over (tap, c_in) W[c_out][tap, c_in] * X[m + tap_off][c_in]
-// with M = 128 output channels per tile and N = BN time rows (64, 128 or 256).
+// with M = 128 output channels per tile and N = BN time rows (64, 128, 192 or 256).
 // Activations are [T, Cp] channels-last 16-bit planes (Cp = C_in rounded up to
 // 64, zero padded); weights are [rows, taps*Cp] with rows = phases*C_out
 // rounded up to a multiple of 128.  FP32 semantics use three bf16 products per
@@ -51,6 +51,8 @@ struct ConvArgs {
                           // (with residual row 0): reflection pad (1, 0) of the ConvTranspose output
     uint32_t* err;        // device error word
     // filled by conv_tc_launch
+    int k_split;          // > 1: the reduction is split over k_split CTAs per tile (see conv_tc_launch)
+    float* part_out;      // split-K raw accumulators [k_split][phases*M][C_out]
     int min_off;          // smallest tap offset (the activation tile starts there)
     int act_box;          // activation TMA box rows; the tile is two boxes
     int desc_mode;        // shared-memory descriptor base-offset convention for row-shifted starts
@@ -64,6 +66,13 @@ struct ConvOperands {
     uint64_t act_rows = 0;          // rows of the activation planes (reads beyond are zero: padding)
     uint64_t act_cp = 0;            // Cp (columns = row pitch, elements)
     CUtensorMap w_hi, w_lo;         // w_lo unused in fp16 mode
+    // Optional split-K scratch (device, FP32).  When a launch has too few output
+    // tiles to fill the GPU and a long reduction, the reduction is split across
+    // CTAs that write raw partial accumulators here, and a second kernel sums
+    // them in a fixed order and applies the epilogue.  Launches that may run
+    // concurrently must not share a scratch buffer.
+    float* scratch = nullptr;
+    size_t scratch_bytes = 0;
 };
 
 // Encodes a 2-D K-major tile map (box 64 x box_rows, 128B swizzle) over a
@@ -78,8 +87,11 @@ inline int conv_tc_weight_rows(int rows) { return (rows + CONV_W_ROWS - 1) / CON
 inline int conv_tc_stats_parts(int M, int n_phases) { return (M + STATS_ROWS - 1) / STATS_ROWS * n_phases; }
 
 // Launch; split = three-pass bf16 mode.  n_phases = polyphase count.
+// Enqueues one kernel, or two (split-K partials, then the ordered reduction
+// and epilogue) when ops.scratch is set and the launch has few tiles.
+// `kernels` (nullable) receives the number of kernels enqueued.
 cudaError_t conv_tc_launch(const ConvOperands& ops, const ConvArgs& a, bool split, int n_phases,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int* kernels = nullptr);
 
 // Sets the kernels' dynamic shared-memory limits on the current device (call
 // once per device before the first launch, outside any stream capture).

@@ -48,6 +48,11 @@ void conv(Run& r, const ConvCall& cc) {
     ops.act_cp = (uint64_t)w.Cp;
     ops.w_hi = w.tm_hi;
     ops.w_lo = w.tm_lo;
+    {   // the split-K scratch of this stream
+        const cudaStream_t sts[4] = {r.c->stream, r.c->side, r.c->rb[0], r.c->rb[1]};
+        for (int i = 0; i < 4; i++)
+            if (r.st == sts[i]) { ops.scratch = r.c->splitk[i]; ops.scratch_bytes = rk_ctx::kSplitKBytes; }
+    }
     ConvArgs a{};
     a.M = cc.M;
     a.C_out = w.C_out;
@@ -86,9 +91,10 @@ void conv(Run& r, const ConvCall& cc) {
         c->prof_flops.push_back(2.0 * w.C_in * w.C_out * w.K * rows);
         cudaEventRecord(e0, r.st);
     }
-    cudaError_t e = conv_tc_launch(ops, a, cc.split, w.phases, r.st);
+    int nk = 0;
+    cudaError_t e = conv_tc_launch(ops, a, cc.split, w.phases, r.st, &nk);
     if (e1) cudaEventRecord(e1, r.st);
-    r.c->launches++;
+    r.c->launches += nk;
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "conv_tc", e);
 }
 

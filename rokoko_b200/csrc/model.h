@@ -174,6 +174,10 @@ struct rk_ctx {
                 ev_rb[2] = {nullptr, nullptr};
     bool use_graphs = true;
     uint32_t* err = nullptr;      // device error word
+    // split-K scratch of the conv launcher, one per stream (main, side, rb[0], rb[1]):
+    // convs that may run concurrently never share one
+    static constexpr size_t kSplitKBytes = 16u << 20;
+    float* splitk[4] = {nullptr, nullptr, nullptr, nullptr};
     bool loaded = false;
     std::vector<void*> weight_allocs;
     rk::DecoderW dec;

@@ -6,6 +6,7 @@
 //   [0, 256)          device error word (uint32) + padding
 //   activation planes  rows x Cp 16-bit, hi then lo (split)
 //   weight planes      C_out (padded to a multiple of 128) x taps x Cp 16-bit, hi then lo (split)
+//   split-K scratch    FP32 partial accumulators, only for launches with few output tiles
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -19,7 +20,7 @@ namespace {
 
 struct ConvPlan {
     int T_out, taps, Cp, rows, tap_off[rk::CONV_MAX_TAPS];
-    size_t act_plane, w_plane, total;
+    size_t act_plane, w_plane, scratch, total;
 };
 
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -44,7 +45,11 @@ bool plan_conv(int C_in, int C_out, int T_in, int K, int stride, int pad, int di
     const int planes = precision == RK_PRECISION_FP32 ? 2 : 1;
     p.act_plane = al256((size_t)p.rows * p.Cp * 2);
     p.w_plane = al256((size_t)rk::conv_tc_weight_rows(C_out) * p.taps * p.Cp * 2);
-    p.total = 256 + planes * (p.act_plane + p.w_plane);
+    // launches with fewer 64-row x 128-channel tiles than a B200 has SMs may split their
+    // reduction over up to 8 CTAs (the kernel's limit)
+    const long tiles = (long)((p.T_out + 63) / 64) * ((C_out + 127) / 128);
+    p.scratch = tiles < 148 ? al256((size_t)8 * p.T_out * C_out * 4) : 0;
+    p.total = 256 + planes * (p.act_plane + p.w_plane) + p.scratch;
     return true;
 }
 
@@ -75,6 +80,7 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
     uint8_t* a_lo = a_hi + p.act_plane;
     uint8_t* w_hi = a_hi + (split ? 2 : 1) * p.act_plane;
     uint8_t* w_lo = w_hi + p.w_plane;
+    uint8_t* scratch = w_hi + (split ? 2 : 1) * p.w_plane;
     // the error word reports on this call only
     if (cudaMemsetAsync(err, 0, 4, st) != cudaSuccess) return rk::fail_cuda(RK_ERR_CUDA, "memset");
 
@@ -104,6 +110,8 @@ extern "C" rk_status rk_conv1d_fprop(const float* x, const float* w, const float
         (split && !rk::make_tmap_k64(&ops.w_lo, w_lo, true, wcols, wrows, wcols, rk::CONV_W_ROWS)))
         return rk::fail(RK_ERR_INIT, "rk_conv1d_fprop: tensor map encoding failed");
     if (!split) ops.w_lo = ops.w_hi;
+    ops.scratch = p.scratch ? reinterpret_cast<float*>(scratch) : nullptr;
+    ops.scratch_bytes = p.scratch;
 
     rk::ConvArgs a{};
     a.M = p.T_out; a.C_out = C_out; a.kblocks = p.Cp / 64; a.taps = p.taps;

@@ -473,6 +473,7 @@ struct Loader {
 void free_weights(rk_ctx* c) {
     for (void* p : c->weight_allocs) cudaFree(p);
     c->weight_allocs.clear();
+    for (auto& p : c->splitk) p = nullptr;  // part of weight_allocs
     c->dec = DecoderW{};
     c->front = FrontW{};
     c->has_front = false;
@@ -496,6 +497,16 @@ rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
     } catch (WeightError& e) {
         free_weights(c);
         return fail(RK_ERR_WEIGHTS, e.what());
+    }
+    for (auto& p : c->splitk) {
+        void* d = nullptr;
+        if (cudaMalloc(&d, rk_ctx::kSplitKBytes) != cudaSuccess) {
+            cudaGetLastError();
+            free_weights(c);
+            return fail(RK_ERR_OOM, "split-K scratch");
+        }
+        c->weight_allocs.push_back(d);
+        p = static_cast<float*>(d);
     }
     if (upload_twiddles() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "twiddle upload");
     if (conv_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "conv kernel attributes");

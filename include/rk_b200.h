@@ -116,6 +116,18 @@ RK_API rk_status rk_decode_features_device(rk_ctx* ctx, const float* d_asr, cons
 RK_API rk_status rk_infer(rk_ctx* ctx, const int32_t* tokens, int T, const float* style256, const int32_t* dur_override,
                    int32_t* dur_out, int* L_out, float* pcm_out, size_t pcm_capacity, size_t* n_samples);
 
+/* Batched form (rk_encode + rk_decode; the reference has one utterance per
+ * rokoko_infer call, src/weights.h:402-405).  rk_encode runs the front half of
+ * B utterances: tokens = the B token lists concatenated (T_per_utt[b] each,
+ * incl. BOS/EOS), style [B][256], optional dur_override and dur_out laid out
+ * like tokens, L_out [B] (nullable).  Each utterance's decoder inputs stay on
+ * the device until rk_decode, which decodes every pending utterance in encode
+ * order into pcm (600 * L[b] samples each, concatenated; pcm_capacity must
+ * hold them all), n_samples [B] (nullable), *B_out (nullable). */
+RK_API rk_status rk_encode(rk_ctx* ctx, const int32_t* tokens, const int32_t* T_per_utt, int B, const float* style,
+                           const int32_t* dur_override, int32_t* dur_out, int32_t* L_out);
+RK_API rk_status rk_decode(rk_ctx* ctx, float* pcm_out, size_t pcm_capacity, size_t* n_samples, int* B_out);
+
 /* Stage activations of the last forward (names as the oracle's stage dumps);
  * copies min(count, cap) floats; *count = element count (0 if unknown). */
 RK_API rk_status rk_get_stage(rk_ctx* ctx, const char* name, float* host_dst, size_t cap, size_t* count);

@@ -111,6 +111,36 @@ class Context:
                                    ctypes.byref(L), _fp(pcm), pcm.shape[0], ctypes.byref(n)), "rk_infer")
         return pcm[: n.value].copy(), dur, L.value
 
+    def encode(self, utterances, overrides=True):
+        """rk_encode over a batch: utterances have .tokens, .style (256) and
+        .durations (used as overrides when `overrides`).  Returns (predicted
+        durations per utterance, L per utterance)."""
+        toks = [np.ascontiguousarray(u.tokens, np.int32) for u in utterances]
+        Ts = np.array([t.shape[0] for t in toks], np.int32)
+        tok = np.ascontiguousarray(np.concatenate(toks), np.int32)
+        sty = np.ascontiguousarray(np.stack([np.asarray(u.style, np.float32) for u in utterances]), np.float32)
+        dov = (np.ascontiguousarray(np.concatenate([np.asarray(u.durations, np.int32) for u in utterances]), np.int32)
+               if overrides else None)
+        dur = np.empty(tok.shape[0], np.int32)
+        Ls = np.empty(len(toks), np.int32)
+        lib.check(self._L.rk_encode(self.h, _ip(tok), _ip(Ts), len(toks), _fp(sty),
+                                    _ip(dov) if dov is not None else None, _ip(dur), _ip(Ls)), "rk_encode")
+        offs = np.concatenate([[0], np.cumsum(Ts)])
+        return [dur[offs[i]:offs[i + 1]].copy() for i in range(len(toks))], [int(x) for x in Ls]
+
+    def decode(self, Ls):
+        """rk_decode of every pending utterance; Ls from encode().  Returns PCM per utterance."""
+        total = 600 * int(sum(Ls))
+        pcm = np.empty(max(total, 1), np.float32)
+        ns = (ctypes.c_size_t * max(len(Ls), 1))()
+        B = ctypes.c_int(0)
+        lib.check(self._L.rk_decode(self.h, _fp(pcm), pcm.shape[0], ns, ctypes.byref(B)), "rk_decode")
+        out, off = [], 0
+        for i in range(B.value):
+            out.append(pcm[off:off + ns[i]].copy())
+            off += ns[i]
+        return out
+
     def profile(self, on: bool = True) -> None:
         lib.check(self._L.rk_profile(self.h, int(on)), "rk_profile")
 

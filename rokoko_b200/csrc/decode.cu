@@ -118,10 +118,10 @@ void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, i
 }
 
 void coef(Run& r, const float* stats, int parts, int ld, int col0, const AdaINW& n, int T, const StyleFC& fc,
-          float* out) {
+          Lane& ln) {
     if (!r.ok()) return;
-    adain_coef(stats, parts, ld, col0, n.C, T, fc.out + n.fc_off, fc.out + n.fc_off + n.C, n.norm_w, n.norm_b, out,
-               r.st);
+    adain_coef(stats, parts, ld, col0, n.C, T, fc.out + n.fc_off, fc.out + n.fc_off + n.C, n.norm_w, n.norm_b,
+               ln.coef, ln.coef_tmp, ln.coef_cnt, r.st);
     r.check_launch("adain_coef");
 }
 
@@ -157,7 +157,7 @@ void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* 
     const int To = b.upsample ? 2 * T : T;
     const bool sp = r.split;
     // norm1 -> LeakyReLU(0.2) [-> depthwise ConvTranspose upsample] -> operand
-    coef(r, stats_x, parts_x, ldsx, 0, b.norm1, T, fc, ln.coef);
+    coef(r, stats_x, parts_x, ldsx, 0, b.norm1, T, fc, ln);
     if (b.upsample) {
         if (!r.ok()) return;
         dw_upsample_pack(x, ldx, T, b.din, ln.coef, ln.coef + b.din, 0.2f, b.pool_w, b.pool_b, ln.op.hi, ln.op.lo,
@@ -170,7 +170,7 @@ void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* 
     c1.w = &b.conv1; c1.op = &ln.op; c1.rows_in = To; c1.split = sp; c1.M = To; c1.T_out = To; c1.pad = 1;
     c1.y = w.enc_r1; c1.ldy = b.dout; c1.stats = ln.stats_a; c1.stats_ld = b.dout;
     conv(r, c1);
-    coef(r, ln.stats_a, stats_parts_for(c1), b.dout, 0, b.norm2, To, fc, ln.coef);
+    coef(r, ln.stats_a, stats_parts_for(c1), b.dout, 0, b.norm2, To, fc, ln);
     pack(r, w.enc_r1, b.dout, To, b.dout, ln.op, b.conv2.Cp, sp, ln.coef, nullptr, 0.2f, true);
     // shortcut: 1x1 conv at T rows (nearest upsample commutes with it)
     const float* res = x;
@@ -206,14 +206,14 @@ void resblock1(Run& r, Lane& ln, const ResBlock1W& rb, const float* x0, const fl
     float* nxt[2] = {ln.xa, ln.xb};
     float* nst[2] = {ln.stats_b, ln.stats_c};
     for (int j = 0; j < 3; j++) {
-        coef(r, sx, px, C, 0, rb.adain1[j], T, fc, ln.coef);
+        coef(r, sx, px, C, 0, rb.adain1[j], T, fc, ln);
         pack(r, x, C, T, C, ln.op, rb.convs1[j].Cp, r.split, ln.coef, rb.alpha1[j]);
         ConvCall c1;
         c1.w = &rb.convs1[j]; c1.op = &ln.op; c1.rows_in = T; c1.split = r.split; c1.M = T; c1.T_out = T;
         c1.dil = dil[j]; c1.pad = (K * dil[j] - dil[j]) / 2;
         c1.y = ln.co; c1.ldy = C; c1.stats = ln.stats_a; c1.stats_ld = C;
         conv(r, c1);
-        coef(r, ln.stats_a, parts, C, 0, rb.adain2[j], T, fc, ln.coef);
+        coef(r, ln.stats_a, parts, C, 0, rb.adain2[j], T, fc, ln);
         pack(r, ln.co, C, T, C, ln.op, rb.convs2[j].Cp, r.split, ln.coef, rb.alpha2[j]);
         ConvCall c2;
         c2.w = &rb.convs2[j]; c2.op = &ln.op; c2.rows_in = T; c2.split = r.split; c2.M = T; c2.T_out = T;
@@ -275,6 +275,8 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
         reqs.push_back({&ln->stats_b, stats});
         reqs.push_back({&ln->stats_c, stats});
         reqs.push_back({&ln->coef, 2 * 1152});
+        reqs.push_back({reinterpret_cast<float**>(&ln->coef_tmp), 16 * 1152 * 2 * 2});
+        reqs.push_back({reinterpret_cast<float**>(&ln->coef_cnt), 64});
     }
     size_t total = 0;
     for (auto& q : reqs) total += al(q.n * 4);
@@ -295,6 +297,9 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
         o.first->lo = base + off; off += o.second;
         o.first->plane_bytes = o.second;
     }
+    for (Lane* ln : lanes)
+        if (cudaMemset(ln->coef_cnt, 0, 64 * sizeof(unsigned)) != cudaSuccess)
+            return fail_cuda(RK_ERR_CUDA, "coefficient tickets");
     w.lane[0].st = c->stream;
     w.lane[1].st = c->rb[0];
     w.lane[2].st = c->rb[1];

@@ -56,7 +56,7 @@ void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, i
           const float* coef = nullptr, const float* snake = nullptr, float slope = 0.f, bool lrelu = false,
           int sr_stride = 1, int sr_pad = 0, int rows_dst = -1);
 void coef(Run& r, const float* stats, int parts, int ld, int col0, const AdaINW& n, int T, const StyleFC& fc,
-          float* out);
+          Lane& ln);
 void record(Run& r, const char* name, const float* d, size_t n);
 void record_cols(Run& r, const char* name, const float* d, int rows, int ld, int C);
 void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* stats_x, int parts_x, int ldsx,

@@ -113,6 +113,8 @@ struct Lane {
     float *xa = nullptr, *xb = nullptr, *co = nullptr, *out = nullptr;  // [T][C] fp32
     float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr;   // conv partials
     float* coef = nullptr;                                               // [2][C]
+    double* coef_tmp = nullptr;                                          // adain_coef slice partials
+    unsigned* coef_cnt = nullptr;                                        // adain_coef tickets (zeroed)
     Operand op;
 };
 
@@ -204,4 +206,10 @@ struct rk_ctx {
     std::vector<double> prof_flops;        // algorithmic FLOPs of each timed launch
     double prof_ms_acc = 0.0, prof_flops_acc = 0.0;
     long long prof_launches_acc = 0;
+    // utterances encoded by rk_encode and not yet decoded: decoder inputs in one device buffer each
+    struct Pending {
+        int L, L_b;
+        float* buf;
+    };
+    std::vector<Pending> pending;
 };

@@ -53,6 +53,10 @@ SIGNATURES = [
     ("rk_infer", ctypes.c_int,
      [ctypes.c_void_p, _i32p, ctypes.c_int, _f32p, _i32p, _i32p, ctypes.POINTER(ctypes.c_int), _f32p,
       ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    ("rk_encode", ctypes.c_int,
+     [ctypes.c_void_p, _i32p, _i32p, ctypes.c_int, _f32p, _i32p, _i32p, _i32p]),
+    ("rk_decode", ctypes.c_int,
+     [ctypes.c_void_p, _f32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_int)]),
     ("rk_get_stage", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_char_p, _f32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     ("rk_record_stages", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
@@ -67,12 +71,14 @@ SIGNATURES = [
 
 
 def load():
-    """Load the in-tree shared library (raises if it is missing)."""
+    """Load the in-tree shared library (raises if it is missing).  The
+    environment variable RK_B200_LIBRARY may name another build of it."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m rokoko_b200.build` (no fallback path exists)")
-        L = ctypes.CDLL(LIB_PATH)
+        path = os.environ.get("RK_B200_LIBRARY") or LIB_PATH
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: run `python -m rokoko_b200.build` (no fallback path exists)")
+        L = ctypes.CDLL(path)
         for name, res, args in SIGNATURES:
             try:
                 fn = getattr(L, name)

@@ -121,7 +121,7 @@ void coef(Run& r, const float* stats, int parts, int ld, int col0, const AdaINW&
           Lane& ln) {
     if (!r.ok()) return;
     adain_coef(stats, parts, ld, col0, n.C, T, fc.out + n.fc_off, fc.out + n.fc_off + n.C, n.norm_w, n.norm_b,
-               ln.coef, ln.coef_tmp, ln.coef_cnt, r.st);
+               ln.coef, r.st);
     r.check_launch("adain_coef");
 }
 
@@ -275,8 +275,6 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
         reqs.push_back({&ln->stats_b, stats});
         reqs.push_back({&ln->stats_c, stats});
         reqs.push_back({&ln->coef, 2 * 1152});
-        reqs.push_back({reinterpret_cast<float**>(&ln->coef_tmp), 16 * 1152 * 2 * 2});
-        reqs.push_back({reinterpret_cast<float**>(&ln->coef_cnt), 64});
     }
     size_t total = 0;
     for (auto& q : reqs) total += al(q.n * 4);
@@ -297,9 +295,6 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
         o.first->lo = base + off; off += o.second;
         o.first->plane_bytes = o.second;
     }
-    for (Lane* ln : lanes)
-        if (cudaMemset(ln->coef_cnt, 0, 64 * sizeof(unsigned)) != cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, "coefficient tickets");
     w.lane[0].st = c->stream;
     w.lane[1].st = c->rb[0];
     w.lane[2].st = c->rb[1];

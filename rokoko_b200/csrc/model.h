@@ -113,8 +113,6 @@ struct Lane {
     float *xa = nullptr, *xb = nullptr, *co = nullptr, *out = nullptr;  // [T][C] fp32
     float *stats_a = nullptr, *stats_b = nullptr, *stats_c = nullptr;   // conv partials
     float* coef = nullptr;                                               // [2][C]
-    double* coef_tmp = nullptr;                                          // adain_coef slice partials
-    unsigned* coef_cnt = nullptr;                                        // adain_coef tickets (zeroed)
     Operand op;
 };
 

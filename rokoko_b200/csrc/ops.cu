@@ -49,28 +49,18 @@ __global__ void style_fc_kernel(const float* __restrict__ W, const float* __rest
 
 // block = 32 channels x 32 part-lanes; each lane sums a strided subset of the
 // parts (fixed order), then the 32 lanes are combined in a fixed tree.
-// AdaIN coefficients from per-part column sums (InstanceNorm statistics).
-// Block (x, y) reduces the parts of slice y for 32 channels (double, fixed
-// tree) into tmp[y]; the last slice block of a channel group to finish (atomic
-// ticket) combines the slices in order and writes scale / shift, then resets
-// the ticket for the next launch.  One launch, deterministic.
-constexpr int COEF_MAX_SLICES = 16;
-
 __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, int ld, int col0, int C, int T,
                                   const float* __restrict__ gamma, const float* __restrict__ beta,
                                   const float* __restrict__ nw, const float* __restrict__ nb,
-                                  float* __restrict__ coef, double* __restrict__ tmp, unsigned* __restrict__ cnt) {
+                                  float* __restrict__ coef) {
     __shared__ double sh_s[32][33], sh_q[32][33];
-    __shared__ bool last;
     const int cx = threadIdx.x, py = threadIdx.y;
     const int c = blockIdx.x * 32 + cx;
-    const int slices = gridDim.y, chunk = (parts + slices - 1) / slices;
-    const int p0 = blockIdx.y * chunk, p1 = min(parts, p0 + chunk);
     double s = 0.0, q = 0.0;
     if (c < C) {
-        // four parts per step, loads issued together (fixed summation order per thread)
-        int p = p0 + py;
-        for (; p + 96 < p1; p += 128) {
+        // four parts per step, loads issued together (fixed summation order: p ascending per thread)
+        int p = py;
+        for (; p + 96 < parts; p += 128) {
             const float s0 = stats[(size_t)p * ld + col0 + c], s1 = stats[(size_t)(p + 32) * ld + col0 + c];
             const float s2 = stats[(size_t)(p + 64) * ld + col0 + c], s3 = stats[(size_t)(p + 96) * ld + col0 + c];
             const float q0 = stats[(size_t)(parts + p) * ld + col0 + c];
@@ -80,7 +70,7 @@ __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, in
             s += s0; s += s1; s += s2; s += s3;
             q += q0; q += q1; q += q2; q += q3;
         }
-        for (; p < p1; p += 32) {
+        for (; p < parts; p += 32) {
             s += stats[(size_t)p * ld + col0 + c];
             q += stats[(size_t)(parts + p) * ld + col0 + c];
         }
@@ -95,31 +85,14 @@ __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, in
         }
         __syncthreads();
     }
-    if (py == 0 && c < C) {
-        tmp[((size_t)blockIdx.y * C + c) * 2] = sh_s[0][cx];
-        tmp[((size_t)blockIdx.y * C + c) * 2 + 1] = sh_q[0][cx];
-    }
-    __threadfence();
-    __syncthreads();
-    if (cx == 0 && py == 0) last = atomicAdd(&cnt[blockIdx.x], 1u) == (unsigned)(slices - 1);
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    if (py == 0 && c < C) {
-        double ts = 0.0, tq = 0.0;
-        for (int y = 0; y < slices; y++) {
-            ts += *(volatile double*)&tmp[((size_t)y * C + c) * 2];
-            tq += *(volatile double*)&tmp[((size_t)y * C + c) * 2 + 1];
-        }
-        const double mean_d = ts / T;
-        const double var_d = tq / T - mean_d * mean_d;
-        const float mean = (float)mean_d;
-        const float inv_std = (float)(1.0 / sqrt(var_d + 1e-5));
-        const float g = 1.0f + gamma[c];
-        coef[c] = g * nw[c] * inv_std;
-        coef[C + c] = g * (nb[c] - nw[c] * mean * inv_std) + beta[c];
-    }
-    if (cx == 0 && py == 0) cnt[blockIdx.x] = 0u;
+    if (py != 0 || c >= C) return;
+    const double mean_d = sh_s[0][cx] / T;
+    const double var_d = sh_q[0][cx] / T - mean_d * mean_d;
+    const float mean = (float)mean_d;
+    const float inv_std = (float)(1.0 / sqrt(var_d + 1e-5));
+    const float g = 1.0f + gamma[c];
+    coef[c] = g * nw[c] * inv_std;
+    coef[C + c] = g * (nb[c] - nw[c] * mean * inv_std) + beta[c];
 }
 
 __global__ void col_stats_kernel(const float* __restrict__ x, int ld, int col0, int ncols, int T,
@@ -348,12 +321,9 @@ void style_fc(const float* W, const float* b, const float* s, float* out, int ro
 }
 
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
-                const float* beta, const float* nw, const float* nb, float* coef, double* tmp, unsigned* cnt,
-                cudaStream_t st) {
-    int slices = (parts + 63) / 64;
-    slices = slices < 1 ? 1 : (slices > COEF_MAX_SLICES ? COEF_MAX_SLICES : slices);
-    adain_coef_kernel<<<dim3((C + 31) / 32, slices), dim3(32, 32), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta,
-                                                                            nw, nb, coef, tmp, cnt);
+                const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st) {
+    adain_coef_kernel<<<(C + 31) / 32, dim3(32, 32), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb,
+                                                              coef);
 }
 
 void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_part, float* stats,

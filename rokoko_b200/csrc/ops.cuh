@@ -12,13 +12,9 @@ void style_fc(const float* W, const float* b, const float* s, float* out, int ro
 // stats[(parts+p)*ld + c] (squares), c in [col0, col0+C).
 //   mean = S/T, var = Q/T - mean^2, inv = 1/sqrt(var + 1e-5)
 //   scale = (1+gamma) w inv;  shift = (1+gamma)(b - w mean inv) + beta
-// written to coef[0..C) (scale) and coef[C..2C) (shift).  One launch: tmp
-// (16 * C * 2 doubles) holds per-slice partials, cnt (ceil(C/32) counters,
-// zero between launches) the tickets; neither may be shared by launches that
-// can run concurrently.
+// written to coef[0..C) (scale) and coef[C..2C) (shift).
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
-                const float* beta, const float* norm_w, const float* norm_b, float* coef, double* tmp,
-                unsigned* cnt, cudaStream_t st);
+                const float* beta, const float* norm_w, const float* norm_b, float* coef, cudaStream_t st);
 
 // Column sums / squares of x[T, ld] columns [col0, col0+ncols) over row blocks
 // of `rows_per_part`, written as stats[p*ld + c] / stats[(parts+p)*ld + c].

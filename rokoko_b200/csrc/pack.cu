@@ -7,8 +7,6 @@
 // writes the conv's operand directly, channel-padded to a multiple of 64.
 // Split mode writes hi = bf16(v) and lo = bf16(v - hi), so that
 // hi*Whi + hi*Wlo + lo*Whi reproduces an FP32 product to ~2^-16 relative.
-#include <cstring>
-
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -68,70 +66,41 @@ __global__ void pack_act_kernel(PackArgs a) {
     }
 }
 
-// Fast path: plain rows (no super-row gather), C a multiple of 8.  One item =
-// 8 channels of one row: two float4 loads, one 16-byte store per plane.  Each
-// thread takes two items per step, both loads in flight before the math.
-template <typename T2>
-__device__ __forceinline__ uint32_t bits2(T2 v) {
-    uint32_t u;
-    memcpy(&u, &v, 4);
-    return u;
-}
-
-template <bool SPLIT>
-__device__ __forceinline__ void pack_store8(const PackArgs& a, long idx, const float* v) {
-    if (SPLIT) {
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-            const float2 hf = __bfloat1622float2(h2);
-            hw[k] = bits2(h2);
-            lw[k] = bits2(__floats2bfloat162_rn(v[2 * k] - hf.x, v[2 * k + 1] - hf.y));
-        }
-        reinterpret_cast<uint4*>(a.hi)[idx] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        reinterpret_cast<uint4*>(a.lo)[idx] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    } else {
-        uint32_t hw[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) hw[k] = bits2(__floats2half2_rn(v[2 * k], v[2 * k + 1]));
-        reinterpret_cast<uint4*>(a.hi)[idx] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    }
-}
-
+// Fast path: plain rows (no super-row gather), C a multiple of 8.  One thread
+// = 8 channels of one row: two float4 loads, one 16-byte store per plane.
 template <bool SPLIT>
 __global__ void pack_act_vec_kernel(PackArgs a) {
     const int groups = a.Cp >> 3, cgroups = a.C >> 3;
     const long total = (long)a.rows_dst * groups;
-    const long stride = (long)gridDim.x * blockDim.x;
-    for (long base = (long)blockIdx.x * blockDim.x + threadIdx.x; base < total; base += 2 * stride) {
-        float v[2][8];
-        int gg[2];
+    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+        const int q = (int)(idx / groups);
+        const int g = (int)(idx - (long)q * groups);
+        float v[8];
+        if (g < cgroups && q < a.rows_src) {
+            const float4* src = reinterpret_cast<const float4*>(a.x + (long)q * a.ldx + g * 8);
+            const float4 p0 = src[0], p1 = src[1];
+            v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+            v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const long idx = base + u * stride;
-            const int q = (int)(idx / groups);
-            const int g = (int)(idx - (long)q * groups);
-            gg[u] = g;
-            if (idx < total && g < cgroups && q < a.rows_src) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + (long)q * a.ldx + g * 8);
-                const float4 p0 = src[0], p1 = src[1];
-                v[u][0] = p0.x; v[u][1] = p0.y; v[u][2] = p0.z; v[u][3] = p0.w;
-                v[u][4] = p1.x; v[u][5] = p1.y; v[u][6] = p1.z; v[u][7] = p1.w;
-            } else {
-                gg[u] = -1;
+            for (int j = 0; j < 8; j++) v[j] = act_transform(v[j], g * 8 + j, a);
+        } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++) v[u][j] = 0.0f;
-            }
+            for (int j = 0; j < 8; j++) v[j] = 0.0f;
         }
+        if (SPLIT) {
+            __align__(16) __nv_bfloat16 h[8], l[8];
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const long idx = base + u * stride;
-            if (gg[u] >= 0) {
-#pragma unroll
-                for (int j = 0; j < 8; j++) v[u][j] = act_transform(v[u][j], gg[u] * 8 + j, a);
+            for (int j = 0; j < 8; j++) {
+                h[j] = __float2bfloat16_rn(v[j]);
+                l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
             }
-            if (idx < total) pack_store8<SPLIT>(a, idx, v[u]);
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
+            reinterpret_cast<uint4*>(a.lo)[idx] = *reinterpret_cast<uint4*>(l);
+        } else {
+            __align__(16) __half h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+            reinterpret_cast<uint4*>(a.hi)[idx] = *reinterpret_cast<uint4*>(h);
         }
     }
 }

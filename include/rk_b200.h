@@ -139,13 +139,30 @@ RK_API rk_status rk_kernel_count(rk_ctx* ctx, long long* count, int reset);
 /* The CUDA stream (cudaStream_t) all of ctx's work is enqueued on. */
 RK_API void* rk_stream(rk_ctx* ctx);
 
-/* Conv profiling: when on, decodes launch eagerly (no CUDA graph) and every
- * tcgen05 conv launch is bracketed by CUDA events on its stream.
- * rk_profile_read synchronises and returns the summed device time (ms), the
- * summed algorithmic FLOPs (2 C_in C_out K T_out; T_in for ConvTranspose1d) and
- * the launch count since rk_profile(ctx, 1). */
-RK_API rk_status rk_profile(rk_ctx* ctx, int on);
+/* Profiling.  rk_profile(ctx, mode) with mode != 0 makes decodes launch
+ * eagerly (no CUDA graph); mode is a set of RK_PROFILE_* bits (1 = the
+ * original "on"):
+ *   RK_PROFILE_CONV      every tcgen05 conv launch is bracketed by CUDA events
+ *                        on its stream; rk_profile_read synchronises and returns
+ *                        the summed device time (ms), the summed algorithmic
+ *                        FLOPs (2 C_in C_out K T_out; T_in for ConvTranspose1d)
+ *                        and the launch count since rk_profile was called.
+ *   RK_PROFILE_SERIAL    every launch of the decode goes to the context stream
+ *                        (no concurrent lanes), so per-launch times are the
+ *                        kernels' own.
+ *   RK_PROFILE_TIMELINE  one CUDA event after every launch.  rk_profile_timeline
+ *                        synchronises and writes one text line per launch,
+ *                        "<stream>\t<name>\t<end ms>", end times relative to the
+ *                        start of the decode (stream 0 = context stream, 1 = the
+ *                        noise branch, 2-3 = resblock lanes); *len = bytes
+ *                        needed (the text is cut at cap - 1 and NUL-terminated);
+ *                        a call with a buffer then forgets the marks. */
+#define RK_PROFILE_CONV 1
+#define RK_PROFILE_SERIAL 2
+#define RK_PROFILE_TIMELINE 4
+RK_API rk_status rk_profile(rk_ctx* ctx, int mode);
 RK_API rk_status rk_profile_read(rk_ctx* ctx, double* conv_ms, double* conv_flops, long long* conv_launches);
+RK_API rk_status rk_profile_timeline(rk_ctx* ctx, char* buf, size_t cap, size_t* len);
 
 RK_API size_t rk_compute_decode_bytes(int T, int L);
 

@@ -17,6 +17,10 @@ from . import lib
 
 FP32 = lib.RK_PRECISION_FP32
 FP16 = lib.RK_PRECISION_FP16
+# rk_profile mode bits (include/rk_b200.h)
+RK_PROFILE_CONV = 1
+RK_PROFILE_SERIAL = 2
+RK_PROFILE_TIMELINE = 4
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -141,8 +145,21 @@ class Context:
             off += ns[i]
         return out
 
-    def profile(self, on: bool = True) -> None:
+    def profile(self, on=True) -> None:
+        """on: False / True (conv events) or a set of RK_PROFILE_* bits (CONV 1, SERIAL 2, TIMELINE 4)."""
         lib.check(self._L.rk_profile(self.h, int(on)), "rk_profile")
+
+    def profile_timeline(self):
+        """[(stream, name, end_ms)] of every launch since the last call (RK_PROFILE_TIMELINE)."""
+        n = ctypes.c_size_t(0)
+        lib.check(self._L.rk_profile_timeline(self.h, None, 0, ctypes.byref(n)), "rk_profile_timeline")
+        buf = ctypes.create_string_buffer(max(n.value, 1))
+        lib.check(self._L.rk_profile_timeline(self.h, buf, len(buf), ctypes.byref(n)), "rk_profile_timeline")
+        out = []
+        for line in buf.value.decode().splitlines():
+            sid, name, t = line.split("\t")
+            out.append((int(sid), name, float(t)))
+        return out
 
     def profile_read(self):
         """(conv device ms, conv algorithmic FLOPs, conv launches) since profile(True)."""

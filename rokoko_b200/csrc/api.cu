@@ -3,6 +3,7 @@
 // rk_decode_features* = the decode phase of rokoko_infer (src/rokoko.cpp:915-1290)
 // on caller-given features; rk_infer adds the front half (src/rokoko.cpp:829-914).
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -97,6 +98,7 @@ extern "C" void rk_destroy(rk_ctx* c) {
     free_front_ws(c);
     free_weights(c);
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
+    for (cudaEvent_t e : c->tl_events) cudaEventDestroy(e);
     if (c->err) cudaFree(c->err);
     cudaEvent_t evs[] = {c->ev_fork, c->ev_join, c->ev_src[0], c->ev_src[1], c->ev_u, c->ev_rb[0], c->ev_rb[1]};
     for (cudaEvent_t e : evs)
@@ -191,7 +193,11 @@ extern "C" void* rk_stream(rk_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
 extern "C" rk_status rk_profile(rk_ctx* c, int on) {
     if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    if (on & ~(RK_PROFILE_CONV | RK_PROFILE_SERIAL | RK_PROFILE_TIMELINE))
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_profile: unknown mode bits");
     c->profile = on != 0;
+    c->prof_mode = on;
+    c->tl_meta.clear();
     c->prof_used = 0;
     c->prof_flops.clear();
     c->prof_ms_acc = 0.0;
@@ -217,6 +223,31 @@ extern "C" rk_status rk_profile_read(rk_ctx* c, double* conv_ms, double* conv_fl
     if (conv_ms) *conv_ms = c->prof_ms_acc;
     if (conv_flops) *conv_flops = c->prof_flops_acc;
     if (conv_launches) *conv_launches = c->prof_launches_acc;
+    return RK_OK;
+}
+
+extern "C" rk_status rk_profile_timeline(rk_ctx* c, char* buf, size_t cap, size_t* len) {
+    if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "null ctx");
+    DeviceGuard g(c->device);
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "rk_profile_timeline sync");
+    std::string out;
+    size_t base = 0;
+    for (size_t i = 0; i < c->tl_meta.size(); i++) {
+        if (c->tl_meta[i].name == "start") base = i;
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, c->tl_events[base], c->tl_events[i]) != cudaSuccess)
+            return fail_cuda(RK_ERR_CUDA, "rk_profile_timeline elapsed");
+        char line[160];
+        snprintf(line, sizeof line, "%d\t%s\t%.4f\n", c->tl_meta[i].stream, c->tl_meta[i].name.c_str(), ms);
+        out += line;
+    }
+    if (len) *len = out.size() + 1;
+    if (buf && cap) {
+        c->tl_meta.clear();
+        const size_t n = out.size() < cap - 1 ? out.size() : cap - 1;
+        memcpy(buf, out.data(), n);
+        buf[n] = 0;
+    }
     return RK_OK;
 }
 

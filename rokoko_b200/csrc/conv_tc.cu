@@ -249,8 +249,8 @@ __global__ void __launch_bounds__(320, 1)
             const uint32_t s_tmem = tmem + acc * C::ACC_STRIDE + ((uint32_t)(wq * 32) << 16);
             // Common case, branch-free so the 32 rows of a chunk interleave: plain
             // residual (no row shift), no activation, no accumulator input, no
-            // duplicated row, and every row of the chunk inside the output.
-            const bool fast_conv = co_ok && !args.act && !args.acc_in && args.res_shift == 0 && args.dup_src_row < 0;
+            // duplicated row in the pair, and every row of the pair inside the output.
+            const bool fast_conv = co_ok && !args.act && !args.acc_in && args.res_shift == 0;
             if (args.part_out) {
                 // split-K: raw accumulators of this reduction slice, rows by m
                 float* po = args.part_out + ((size_t)(ks * n_phases + phase) * args.M) * args.C_out + co;
@@ -264,16 +264,20 @@ __global__ void __launch_bounds__(320, 1)
                         if (mc + j < args.M && co_ok) po[(size_t)(mc + j) * args.C_out] = v[j];
                 }
             }
+            const int n_pairs = (ok && !args.part_out) ? min(BN / 64, (args.M - m0 + 63) / 64) : 0;
 #pragma unroll 1
-            for (int pp = half; pp < ((ok && !args.part_out) ? BN / 64 : 0); pp += 2) {
+            for (int pp = half; pp < n_pairs; pp += 2) {
                 float s = 0.f, q = 0.f;
                 const int mp = m0 + pp * 64;
                 const int orow_p = mp * args.o_stride + args.o_off + phase * args.o_phase_step;
                 const int orow_last = orow_p + 63 * args.o_stride;
                 // warp-uniform: tcgen05.ld below is a .sync.aligned instruction, so every lane
                 // of the warp must take the same path (lanes past C_out take the general one)
-                const bool fast = __all_sync(0xffffffffu, fast_conv && mp + 63 < args.M && orow_p >= args.o_min &&
-                                                              orow_last < args.T_out);
+                // the reflection-pad duplicate row, if this pair holds it, takes the general path
+                const bool has_dup = args.dup_src_row >= orow_p && args.dup_src_row <= orow_last &&
+                                     (args.dup_src_row - orow_p) % args.o_stride == 0;
+                const bool fast = __all_sync(0xffffffffu, fast_conv && !has_dup && mp + 63 < args.M &&
+                                                              orow_p >= args.o_min && orow_last < args.T_out);
                 if (fast) {
                     // residual rows of both chunks in flight before the accumulator reads
                     const size_t rstep = (size_t)args.o_stride * args.ldres, ystep = (size_t)args.o_stride * args.ldy;
@@ -303,47 +307,32 @@ __global__ void __launch_bounds__(320, 1)
                         }
                     }
                 } else {
+                    // General path (partial chunks, row-shifted residual, GELU, accumulator
+                    // input, the reflection-pad duplicate): one TMEM column per valid row, a
+                    // rolled loop so that the rarely executed code stays small.  Row validity
+                    // is warp-uniform, so every lane takes the same tcgen05.ld.
 #pragma unroll 1
-                    for (int cc = 0; cc < 2; cc++) {
-                        const int c = 2 * pp + cc;
-                        const int mc = m0 + c * 32;
-                        const int orow0 = mc * args.o_stride + args.o_off + phase * args.o_phase_step;
-                        float rv[32];
-#pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const int orow = orow0 + j * args.o_stride;
-                            const bool val = co_ok && mc + j < args.M && orow >= args.o_min && orow < args.T_out;
-                            rv[j] = (args.res && val) ? args.res[(size_t)(orow >> args.res_shift) * args.ldres + co]
-                                                      : 0.f;
-                        }
-                        float v[32];
-                        tmem_ld32(s_tmem + (uint32_t)(c * 32), v);
-#pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const int orow = orow0 + j * args.o_stride;
-                            if (!(co_ok && mc + j < args.M && orow >= args.o_min && orow < args.T_out)) continue;
-                            float o = v[j];
-                            if (args.res) o += rv[j];
+                    for (int j = 0; j < 64; j++) {
+                        const int m = mp + j;
+                        const int orow = orow_p + j * args.o_stride;
+                        if (m >= args.M || orow < args.o_min || orow >= args.T_out) continue;
+                        const float acc = tmem_ld1(s_tmem + (uint32_t)(2 * pp * 32 + j));
+                        if (!co_ok) continue;
+                        for (int pass = 0; pass < 2; pass++) {
+                            // pass 1: reflection pad (1, 0), the accumulator of dup_src_row also
+                            // goes to row 0 with residual / accumulator row 0
+                            if (pass == 1 && orow != args.dup_src_row) break;
+                            const int orw = pass ? 0 : orow;
+                            const int rrow = pass ? 0 : (orow >> args.res_shift);
+                            float o = acc;
+                            if (args.res) o += args.res[(size_t)rrow * args.ldres + co];
                             o += bias_v;
                             if (args.act == 1) o = gelu_tanh(o);
-                            if (args.acc_in) o = args.acc_in[(size_t)orow * args.ldacc + co] + o;
+                            if (args.acc_in) o = args.acc_in[(size_t)orw * args.ldacc + co] + o;
                             o *= args.alpha;
-                            args.y[(size_t)orow * args.ldy + co] = o;
+                            args.y[(size_t)orw * args.ldy + co] = o;
                             s += o;
                             q += o * o;
-                            // reflection pad (1, 0): the accumulator of dup_src_row also goes to
-                            // row 0, with residual / accumulator row 0
-                            if (orow == args.dup_src_row) {
-                                float o0 = v[j];
-                                if (args.res) o0 += args.res[co];
-                                o0 += bias_v;
-                                if (args.act == 1) o0 = gelu_tanh(o0);
-                                if (args.acc_in) o0 = args.acc_in[co] + o0;
-                                o0 *= args.alpha;
-                                args.y[co] = o0;
-                                s += o0;
-                                q += o0 * o0;
-                            }
                         }
                     }
                 }
@@ -517,7 +506,11 @@ cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_pha
 // tile streamed from L2 feeds BN rows: measured on B200 about full rate at
 // BN = 256, 70 % at 128, 40 % at 64), plus the split-K second pass (partials
 // written and read once at about 4 TB/s).  Only BN whose activation ring fits
-// in shared memory are considered.
+// in shared memory are considered.  Long launches (M >= 4096 rows: the
+// generator's resblocks, which run three at a time on concurrent streams)
+// minimise SM-time instead of waves: the partial last wave of one launch is
+// filled by CTAs of the others (measured on the config-1 decode graph: BN =
+// 256 for these launches, 2.53 -> 2.40 ms).
 void pick_tiling(const ConvArgs& a, int n_phases, int halo, bool split, const ConvOperands& ops, int* bn_out,
                  int* ks_out) {
     const int ctiles = (a.C_out + CONV_W_ROWS - 1) / CONV_W_ROWS * n_phases;
@@ -531,6 +524,7 @@ void pick_tiling(const ConvArgs& a, int n_phases, int halo, bool split, const Co
     double best = 1e30;
     *bn_out = 0;
     *ks_out = 1;
+    const bool sm_time = a.M >= 4096;
     for (int i = 0; i < 4; i++) {
         const int bn = cands[i];
         const int box = act_box_rows(bn, halo);
@@ -538,13 +532,13 @@ void pick_tiling(const ConvArgs& a, int n_phases, int halo, bool split, const Co
         if (ws < 2 || box > 256) continue;
         const int tiles = (a.M + bn - 1) / bn * ctiles;
         int kmax = 1;
-        if (ops.scratch && a.kblocks >= 4) {
+        if (ops.scratch && a.kblocks >= 4 && !sm_time) {
             kmax = a.kblocks / 2 < MAX_K_SPLIT ? a.kblocks / 2 : MAX_K_SPLIT;
             while (kmax > 1 && (size_t)kmax * slice_bytes > ops.scratch_bytes) kmax--;
         }
         for (int ks = 1; ks <= kmax; ks++) {
             const int units = tiles * ks;
-            const int waves = (units + sms - 1) / sms;
+            const double waves = sm_time ? (double)units / sms : (double)((units + sms - 1) / sms);
             const double unit_us = (double)bn * a.taps * ((a.kblocks + ks - 1) / ks) / (tc_rows_per_us * eff[i]);
             double t = waves * unit_us;
             if (ks > 1) t += 2.0 * ks * slice_bytes / 4.0e6 + 3.0;  // second pass + its launch

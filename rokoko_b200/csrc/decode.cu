@@ -17,6 +17,7 @@
 //   lanes 1, 2  : resblocks 3i+1, 3i+2 (independent of resblock 3i)
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 
 #include "decode.h"
@@ -31,6 +32,22 @@ namespace rk {
 
 
 int stats_parts_for(const ConvCall& cc) { return conv_tc_stats_parts(cc.M, cc.w->phases); }
+
+void tl_mark(rk_ctx* c, cudaStream_t st, const char* name) {
+    if (!c->profile || !(c->prof_mode & RK_PROFILE_TIMELINE)) return;
+    const size_t i = c->tl_meta.size();
+    if (c->tl_events.size() <= i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) { cudaGetLastError(); return; }
+        c->tl_events.push_back(e);
+    }
+    int sid = 0;
+    if (st == c->side) sid = 1;
+    else if (st == c->rb[0]) sid = 2;
+    else if (st == c->rb[1]) sid = 3;
+    if (cudaEventRecord(c->tl_events[i], st) != cudaSuccess) { cudaGetLastError(); return; }
+    c->tl_meta.push_back({sid, name});
+}
 
 void conv(Run& r, const ConvCall& cc) {
     if (!r.ok()) return;
@@ -77,7 +94,7 @@ void conv(Run& r, const ConvCall& cc) {
     a.err = r.c->err;
     rk_ctx* c = r.c;
     cudaEvent_t e1 = nullptr;
-    if (c->profile) {
+    if (c->profile && (c->prof_mode & RK_PROFILE_CONV)) {
         while (c->prof_events.size() < c->prof_used + 2) {
             cudaEvent_t evt;
             if (cudaEventCreate(&evt) != cudaSuccess) { r.status = fail_cuda(RK_ERR_CUDA, "profile event"); return; }
@@ -89,12 +106,19 @@ void conv(Run& r, const ConvCall& cc) {
         // algorithmic FLOPs: 2 C_in C_out K T_out (ConvTranspose1d: x T_in)
         const double rows = w.phases > 1 ? (double)cc.rows_in : (double)cc.T_out;
         c->prof_flops.push_back(2.0 * w.C_in * w.C_out * w.K * rows);
-        cudaEventRecord(e0, r.st);
+        // external: inside a stream capture the record becomes an event node of the graph
+        cudaEventRecordWithFlags(e0, r.st, cudaEventRecordExternal);
     }
     int nk = 0;
     cudaError_t e = conv_tc_launch(ops, a, cc.split, w.phases, r.st, &nk);
-    if (e1) cudaEventRecord(e1, r.st);
+    if (e1) cudaEventRecordWithFlags(e1, r.st, cudaEventRecordExternal);
     r.c->launches += nk;
+    if (c->profile && (c->prof_mode & RK_PROFILE_TIMELINE)) {
+        char nm[96];
+        snprintf(nm, sizeof nm, "conv %d>%d K%d d%d T%d%s", w.C_in, w.C_out, w.K, cc.dil, cc.T_out,
+                 w.phases > 1 ? " convT" : "");
+        tl_mark(c, r.st, nm);
+    }
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "conv_tc", e);
 }
 
@@ -114,6 +138,7 @@ void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, i
     }
     cudaError_t e = pack_act(a, split, r.st);
     r.c->launches++;
+    tl_mark(r.c, r.st, coef ? (snake ? "pack_adain_snake" : "pack_adain_lrelu") : "pack");
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "pack_act", e);
 }
 
@@ -310,13 +335,18 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     const DecoderW& d = c->dec;
     const int L2 = 2 * L, T1 = 20 * L, T2 = 120 * L + 1, TA = 600 * L;
     const bool sp = c->precision == RK_PRECISION_FP32;
+    // RK_PROFILE_SERIAL: every lane on the context stream
+    const bool serial = c->profile && (c->prof_mode & RK_PROFILE_SERIAL);
+    const cudaStream_t side = serial ? c->stream : c->side;
+    const cudaStream_t lane1 = serial ? c->stream : c->rb[0], lane2 = serial ? c->stream : c->rb[1];
     Run r{c, c->stream, sp};
-    Run s{c, c->side, sp};
+    Run s{c, side, sp};
+    tl_mark(c, c->stream, "start");
 
     // style FCs first (the noise branch needs them too)
     style_fc(d.fc.w, d.fc.b, w.style, d.fc.out, d.fc.rows, r.st);
     r.check_launch("style_fc");
-    if (!ev(cudaEventRecord(c->ev_fork, r.st)) || !ev(cudaStreamWaitEvent(c->side, c->ev_fork, 0)))
+    if (!ev(cudaEventRecord(c->ev_fork, r.st)) || !ev(cudaStreamWaitEvent(side, c->ev_fork, 0)))
         return fail_cuda(RK_ERR_CUDA, "fork");
 
     // ---- side stream: SineGen -> STFT -> noise branches (depend on F0 only)
@@ -405,17 +435,17 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
         const int parts_u = stats_parts_for(cu);
         record(r, i == 0 ? "gen0_ups" : "gen1_ups", w.u, (size_t)Tu * Co);
         // the three resblocks run concurrently on lanes 0, 1, 2
-        if (!ev(cudaEventRecord(c->ev_u, r.st)) || !ev(cudaStreamWaitEvent(c->rb[0], c->ev_u, 0)) ||
-            !ev(cudaStreamWaitEvent(c->rb[1], c->ev_u, 0)))
+        if (!ev(cudaEventRecord(c->ev_u, r.st)) || !ev(cudaStreamWaitEvent(lane1, c->ev_u, 0)) ||
+            !ev(cudaStreamWaitEvent(lane2, c->ev_u, 0)))
             return fail_cuda(RK_ERR_CUDA, "fork resblocks");
-        Run lr[3] = {r, Run{c, c->rb[0], sp}, Run{c, c->rb[1], sp}};
+        Run lr[3] = {r, Run{c, lane1, sp}, Run{c, lane2, sp}};
         for (int j = 0; j < 3; j++)
             resblock1(lr[j], w.lane[j], d.resblocks[i * 3 + j], w.u, w.stats_u, parts_u, Tu, w.lane[j].out, d.fc);
         r = lr[0];
         r.merge(lr[1]);
         r.merge(lr[2]);
         for (int j = 0; j < 2; j++)
-            if (!ev(cudaEventRecord(c->ev_rb[j], c->rb[j])) || !ev(cudaStreamWaitEvent(r.st, c->ev_rb[j], 0)))
+            if (!ev(cudaEventRecord(c->ev_rb[j], lr[j + 1].st)) || !ev(cudaStreamWaitEvent(r.st, c->ev_rb[j], 0)))
                 return fail_cuda(RK_ERR_CUDA, "join resblocks");
         if (!r.ok()) return r.status;
         // ((rb0 + rb1) + rb2) / 3 -> LeakyReLU(0.1) -> ups[1] operand, or LeakyReLU(0.01) -> conv_post operand
@@ -424,6 +454,7 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
         cudaError_t e = pack_avg3(w.lane[0].out, w.lane[1].out, w.lane[2].out, Tu, Co, nextw.Cp,
                                   i == 0 ? 0.1f : 0.01f, nop.hi, nop.lo, sp, c->record ? w.avg : nullptr, r.st);
         c->launches++;
+        tl_mark(c, r.st, "pack_avg3");
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_LAUNCH, "pack_avg3", e);
         record(r, i == 0 ? "gen0_out" : "gen1_out", w.avg, (size_t)Tu * Co);
         Tl = Tu;
@@ -442,28 +473,47 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     return r.status;
 }
 
-// One CUDA graph per L.  Stage recording and conv profiling (per-launch
-// timing events) run the same launch sequence eagerly.
+// One CUDA graph per L.  Stage recording and the timeline profile run the same
+// launch sequence eagerly; conv profiling (RK_PROFILE_CONV, optionally with
+// RK_PROFILE_SERIAL) is captured into its own graph whose conv timing events
+// are event nodes, so that each replay re-records them.
 rk_status enqueue_decode(rk_ctx* c, int L) {
-    if (c->record || c->profile || !c->use_graphs) return enqueue_decode_body(c, L);
-    const std::pair<int, bool> key{L, false};
+    const bool prof_graph = c->profile && (c->prof_mode & RK_PROFILE_CONV) && !(c->prof_mode & RK_PROFILE_TIMELINE);
+    if (c->record || (c->profile && !prof_graph) || !c->use_graphs) return enqueue_decode_body(c, L);
+    const std::pair<int, int> key{L, prof_graph ? c->prof_mode : 0};
     auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
         const long long before = c->launches;
+        // conv timing events of a profiling capture start at the front of the pool
+        const size_t used0 = c->prof_used;
+        std::vector<double> flops0;
+        if (prof_graph) { flops0.swap(c->prof_flops); c->prof_used = 0; }
         if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
             return fail_cuda(RK_ERR_CUDA, "graph capture begin");
         rk_status s = enqueue_decode_body(c, L);
         cudaGraph_t g = nullptr;
         cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+        rk_ctx::GraphRec rec;
+        if (prof_graph) {
+            rec.prof_events = c->prof_used;
+            rec.prof_flops.swap(c->prof_flops);
+            c->prof_used = used0;
+            c->prof_flops.swap(flops0);
+        }
         if (s != RK_OK) { if (g) cudaGraphDestroy(g); cudaGetLastError(); return s; }
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "graph capture end", e);
-        rk_ctx::GraphRec rec;
         e = cudaGraphInstantiateWithFlags(&rec.exec, g, 0);
         cudaGraphDestroy(g);
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "graph instantiate", e);
         rec.launches = c->launches - before;
         c->launches = before;
         it = c->graphs.emplace(key, std::move(rec)).first;
+    }
+    if (prof_graph) {
+        // the replay re-records the graph's event pairs: earlier pairs must have been read
+        if (c->prof_used != 0) return fail(RK_ERR_STATE, "rk_profile_read must follow each profiled decode");
+        c->prof_used = it->second.prof_events;
+        c->prof_flops = it->second.prof_flops;
     }
     cudaError_t e = cudaGraphLaunch(it->second.exec, c->stream);
     if (e != cudaSuccess) return fail_cuda_err(RK_ERR_LAUNCH, "graph launch", e);

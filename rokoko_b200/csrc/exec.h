@@ -10,6 +10,10 @@
 
 namespace rk {
 
+// Timeline mark (rk_profile with RK_PROFILE_TIMELINE): records an event on `st`
+// after the launch just enqueued; a no-op otherwise.
+void tl_mark(rk_ctx* c, cudaStream_t st, const char* name);
+
 struct Run {
     rk_ctx* c;
     cudaStream_t st;
@@ -19,6 +23,7 @@ struct Run {
     bool ok() const { return status == RK_OK; }
     void check_launch(const char* what) {
         c->launches++;
+        tl_mark(c, st, what);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess && status == RK_OK) status = fail_cuda_err(RK_ERR_LAUNCH, what, e);
     }

@@ -188,17 +188,23 @@ struct rk_ctx {
     bool record = false;
     std::map<std::string, rk::StageRec> stages;
     long long launches = 0;
-    // decode graphs keyed by (L, profiling): the executable, the kernel count
-    // it replays, and (profiling variant) the conv timing events it records
+    // decode graphs keyed by (L, profiling mode): the executable, the kernel
+    // count it replays, and (profiling variant) the conv timing events it records
     struct GraphRec {
         cudaGraphExec_t exec = nullptr;
         long long launches = 0;
         size_t prof_events = 0;
         std::vector<double> prof_flops;
     };
-    std::map<std::pair<int, bool>, GraphRec> graphs;
-    // conv profiling (rk_profile): event pairs around each conv launch
+    std::map<std::pair<int, int>, GraphRec> graphs;
+    // profiling (rk_profile): mode bits RK_PROFILE_*; event pairs around each conv launch
     bool profile = false;
+    int prof_mode = 0;
+    // timeline (RK_PROFILE_TIMELINE): one event after every launch, with its stream and name;
+    // event 0 of a decode is the "start" mark on the context stream
+    std::vector<cudaEvent_t> tl_events;
+    struct TlMark { int stream; std::string name; };
+    std::vector<TlMark> tl_meta;
     std::vector<cudaEvent_t> prof_events;  // pool, 2 per launch
     size_t prof_used = 0;
     std::vector<double> prof_flops;        // algorithmic FLOPs of each timed launch

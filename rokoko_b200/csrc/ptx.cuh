@@ -132,6 +132,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// One TMEM column per lane (32 lanes x 32 bit): the compact form of tmem_ld32
+// for paths that read a few scattered columns.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return __uint_as_float(r);
+}
+
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
 // layout written by TMA with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), leading offset unused (1), descriptor

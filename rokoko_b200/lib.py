@@ -67,6 +67,8 @@ SIGNATURES = [
     ("rk_profile_read", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
       ctypes.POINTER(ctypes.c_longlong)]),
+    ("rk_profile_timeline", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
 ]
 
 

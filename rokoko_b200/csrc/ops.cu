@@ -49,28 +49,33 @@ __global__ void style_fc_kernel(const float* __restrict__ W, const float* __rest
 
 // block = 32 channels x 32 part-lanes; each lane sums a strided subset of the
 // parts (fixed order), then the 32 lanes are combined in a fixed tree.
-__global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, int ld, int col0, int C, int T,
-                                  const float* __restrict__ gamma, const float* __restrict__ beta,
-                                  const float* __restrict__ nw, const float* __restrict__ nb,
-                                  float* __restrict__ coef) {
-    __shared__ double sh_s[32][33], sh_q[32][33];
+// AdaIN coefficients from the InstanceNorm partials: block = 8 channels x 128
+// part slices; slice y sums parts y, y + 128, ... in double (loads in flight
+// together), then a fixed-order halving tree over the slices.  mean = S / T,
+// var = Q / T - mean^2 (biased, the reference's single-pass form), scale =
+// (1 + gamma) w / sqrt(var + 1e-5), shift = (1 + gamma)(b - w mean / sqrt(var + eps)) + beta.
+__global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restrict__ stats, int parts, int ld,
+                                                          int col0, int C, int T, const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta,
+                                                          const float* __restrict__ nw,
+                                                          const float* __restrict__ nb, float* __restrict__ coef) {
+    __shared__ double sh_s[128][8], sh_q[128][8];
     const int cx = threadIdx.x, py = threadIdx.y;
-    const int c = blockIdx.x * 32 + cx;
+    const int c = blockIdx.x * 8 + cx;
     double s = 0.0, q = 0.0;
     if (c < C) {
-        // four parts per step, loads issued together (fixed summation order: p ascending per thread)
         int p = py;
-        for (; p + 96 < parts; p += 128) {
-            const float s0 = stats[(size_t)p * ld + col0 + c], s1 = stats[(size_t)(p + 32) * ld + col0 + c];
-            const float s2 = stats[(size_t)(p + 64) * ld + col0 + c], s3 = stats[(size_t)(p + 96) * ld + col0 + c];
+        for (; p + 384 < parts; p += 512) {
+            const float s0 = stats[(size_t)p * ld + col0 + c], s1 = stats[(size_t)(p + 128) * ld + col0 + c];
+            const float s2 = stats[(size_t)(p + 256) * ld + col0 + c], s3 = stats[(size_t)(p + 384) * ld + col0 + c];
             const float q0 = stats[(size_t)(parts + p) * ld + col0 + c];
-            const float q1 = stats[(size_t)(parts + p + 32) * ld + col0 + c];
-            const float q2 = stats[(size_t)(parts + p + 64) * ld + col0 + c];
-            const float q3 = stats[(size_t)(parts + p + 96) * ld + col0 + c];
+            const float q1 = stats[(size_t)(parts + p + 128) * ld + col0 + c];
+            const float q2 = stats[(size_t)(parts + p + 256) * ld + col0 + c];
+            const float q3 = stats[(size_t)(parts + p + 384) * ld + col0 + c];
             s += s0; s += s1; s += s2; s += s3;
             q += q0; q += q1; q += q2; q += q3;
         }
-        for (; p < parts; p += 32) {
+        for (; p < parts; p += 128) {
             s += stats[(size_t)p * ld + col0 + c];
             q += stats[(size_t)(parts + p) * ld + col0 + c];
         }
@@ -78,7 +83,7 @@ __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, in
     sh_s[py][cx] = s;
     sh_q[py][cx] = q;
     __syncthreads();
-    for (int o = 16; o >= 1; o >>= 1) {
+    for (int o = 64; o >= 1; o >>= 1) {
         if (py < o) {
             sh_s[py][cx] += sh_s[py + o][cx];
             sh_q[py][cx] += sh_q[py + o][cx];
@@ -95,20 +100,36 @@ __global__ void adain_coef_kernel(const float* __restrict__ stats, int parts, in
     coef[C + c] = g * (nb[c] - nw[c] * mean * inv_std) + beta[c];
 }
 
-__global__ void col_stats_kernel(const float* __restrict__ x, int ld, int col0, int ncols, int T,
-                                 int rows_per_part, int parts, float* __restrict__ stats) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// Column sum / sum-of-squares partials per part of rows_per_part rows.  Block
+// = 32 columns x 8 row slices; slice y sums rows y, y + 8, ... of the part
+// (loads independent and in flight together), then slice 0 adds the eight
+// slice sums in order.
+__global__ void __launch_bounds__(256) col_stats_kernel(const float* __restrict__ x, int ld, int col0, int ncols,
+                                                        int T, int rows_per_part, int parts,
+                                                        float* __restrict__ stats) {
+    __shared__ float sh_s[8][32], sh_q[8][32];
+    const int cx = threadIdx.x, sy = threadIdx.y;
+    const int c = blockIdx.x * 32 + cx;
     const int p = blockIdx.y;
-    if (c >= ncols) return;
     const int r0 = p * rows_per_part, r1 = min(T, r0 + rows_per_part);
     float s = 0.f, q = 0.f;
-    for (int r = r0; r < r1; r++) {
-        const float v = x[(size_t)r * ld + col0 + c];
-        s += v;
-        q += v * v;
+    if (c < ncols) {
+#pragma unroll 4
+        for (int r = r0 + sy; r < r1; r += 8) {
+            const float v = x[(size_t)r * ld + col0 + c];
+            s += v;
+            q += v * v;
+        }
     }
-    stats[(size_t)p * ld + col0 + c] = s;
-    stats[(size_t)(parts + p) * ld + col0 + c] = q;
+    sh_s[sy][cx] = s;
+    sh_q[sy][cx] = q;
+    __syncthreads();
+    if (sy != 0 || c >= ncols) return;
+    float ts = 0.f, tq = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) { ts += sh_s[k][cx]; tq += sh_q[k][cx]; }
+    stats[(size_t)p * ld + col0 + c] = ts;
+    stats[(size_t)(parts + p) * ld + col0 + c] = tq;
 }
 
 __global__ void f0n_down_kernel(const float* __restrict__ f0, const float* __restrict__ n,
@@ -322,15 +343,15 @@ void style_fc(const float* W, const float* b, const float* s, float* out, int ro
 
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
                 const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st) {
-    adain_coef_kernel<<<(C + 31) / 32, dim3(32, 32), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb,
-                                                              coef);
+    adain_coef_kernel<<<(C + 7) / 8, dim3(8, 128), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb,
+                                                             coef);
 }
 
 void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_part, float* stats,
                cudaStream_t st) {
     const int parts = (T + rows_per_part - 1) / rows_per_part;
-    dim3 grid((ncols + 127) / 128, parts);
-    col_stats_kernel<<<grid, 128, 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats);
+    dim3 grid((ncols + 31) / 32, parts);
+    col_stats_kernel<<<grid, dim3(32, 8), 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats);
 }
 
 void f0n_down(const float* f0, const float* n, const float* wf, const float* bf, const float* wn, const float* bn,

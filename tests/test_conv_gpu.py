@@ -25,6 +25,12 @@ CASES = [
     # more tiles than SMs: each persistent CTA runs several tiles through both accumulators
     (128, 128, 48001, 7, 1, 9, 3, True),
     (128, 128, 100000, 3, 1, 1, 1, False),
+    # long launches (256-row tiles where the ring fits): widest halo (K 11, dilation 5),
+    # partial last tiles, bias and residual epilogues
+    (128, 128, 48001, 11, 1, 25, 5, False),
+    (256, 256, 8000, 11, 1, 25, 5, True),
+    (256, 256, 5000, 3, 1, 1, 1, False),
+    (128, 128, 4104, 7, 1, 3, 1, True),
 ]
 
 

@@ -139,9 +139,10 @@ RK_API rk_status rk_kernel_count(rk_ctx* ctx, long long* count, int reset);
 /* The CUDA stream (cudaStream_t) all of ctx's work is enqueued on. */
 RK_API void* rk_stream(rk_ctx* ctx);
 
-/* Profiling.  rk_profile(ctx, mode) with mode != 0 makes decodes launch
- * eagerly (no CUDA graph); mode is a set of RK_PROFILE_* bits (1 = the
- * original "on"):
+/* Profiling.  rk_profile(ctx, mode), mode a set of RK_PROFILE_* bits (1 = the
+ * original "on"), makes decodes replay a separate CUDA graph per mode whose
+ * timing events are event nodes (each profiled decode must be read back with
+ * rk_profile_read / rk_profile_timeline before the next one):
  *   RK_PROFILE_CONV      every tcgen05 conv launch is bracketed by CUDA events
  *                        on its stream; rk_profile_read synchronises and returns
  *                        the summed device time (ms), the summed algorithmic
@@ -150,7 +151,7 @@ RK_API void* rk_stream(rk_ctx* ctx);
  *   RK_PROFILE_SERIAL    every launch of the decode goes to the context stream
  *                        (no concurrent lanes), so per-launch times are the
  *                        kernels' own.
- *   RK_PROFILE_TIMELINE  one CUDA event after every launch.  rk_profile_timeline
+ *   RK_PROFILE_TIMELINE  one event node after every launch.  rk_profile_timeline
  *                        synchronises and writes one text line per launch,
  *                        "<stream>\t<name>\t<end ms>", end times relative to the
  *                        start of the decode (stream 0 = context stream, 1 = the

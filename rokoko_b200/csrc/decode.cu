@@ -45,7 +45,11 @@ void tl_mark(rk_ctx* c, cudaStream_t st, const char* name) {
     if (st == c->side) sid = 1;
     else if (st == c->rb[0]) sid = 2;
     else if (st == c->rb[1]) sid = 3;
-    if (cudaEventRecord(c->tl_events[i], st) != cudaSuccess) { cudaGetLastError(); return; }
+    // external: inside a stream capture the record becomes an event node of the graph
+    if (cudaEventRecordWithFlags(c->tl_events[i], st, cudaEventRecordExternal) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
     c->tl_meta.push_back({sid, name});
 }
 
@@ -473,12 +477,12 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     return r.status;
 }
 
-// One CUDA graph per L.  Stage recording and the timeline profile run the same
-// launch sequence eagerly; conv profiling (RK_PROFILE_CONV, optionally with
-// RK_PROFILE_SERIAL) is captured into its own graph whose conv timing events
-// are event nodes, so that each replay re-records them.
+// One CUDA graph per L.  Stage recording runs the same launch sequence eagerly;
+// a profiled decode (RK_PROFILE_CONV and / or RK_PROFILE_TIMELINE, optionally
+// RK_PROFILE_SERIAL) is captured into its own graph whose timing events are
+// event nodes, so that each replay re-records them.
 rk_status enqueue_decode(rk_ctx* c, int L) {
-    const bool prof_graph = c->profile && (c->prof_mode & RK_PROFILE_CONV) && !(c->prof_mode & RK_PROFILE_TIMELINE);
+    const bool prof_graph = c->profile && (c->prof_mode & (RK_PROFILE_CONV | RK_PROFILE_TIMELINE));
     if (c->record || (c->profile && !prof_graph) || !c->use_graphs) return enqueue_decode_body(c, L);
     const std::pair<int, int> key{L, prof_graph ? c->prof_mode : 0};
     auto it = c->graphs.find(key);
@@ -487,7 +491,8 @@ rk_status enqueue_decode(rk_ctx* c, int L) {
         // conv timing events of a profiling capture start at the front of the pool
         const size_t used0 = c->prof_used;
         std::vector<double> flops0;
-        if (prof_graph) { flops0.swap(c->prof_flops); c->prof_used = 0; }
+        std::vector<rk_ctx::TlMark> marks0;
+        if (prof_graph) { flops0.swap(c->prof_flops); c->prof_used = 0; marks0.swap(c->tl_meta); }
         if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
             return fail_cuda(RK_ERR_CUDA, "graph capture begin");
         rk_status s = enqueue_decode_body(c, L);
@@ -497,8 +502,10 @@ rk_status enqueue_decode(rk_ctx* c, int L) {
         if (prof_graph) {
             rec.prof_events = c->prof_used;
             rec.prof_flops.swap(c->prof_flops);
+            rec.tl_marks.swap(c->tl_meta);
             c->prof_used = used0;
             c->prof_flops.swap(flops0);
+            c->tl_meta.swap(marks0);
         }
         if (s != RK_OK) { if (g) cudaGraphDestroy(g); cudaGetLastError(); return s; }
         if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "graph capture end", e);
@@ -511,9 +518,11 @@ rk_status enqueue_decode(rk_ctx* c, int L) {
     }
     if (prof_graph) {
         // the replay re-records the graph's event pairs: earlier pairs must have been read
-        if (c->prof_used != 0) return fail(RK_ERR_STATE, "rk_profile_read must follow each profiled decode");
+        if (c->prof_used != 0 || !c->tl_meta.empty())
+            return fail(RK_ERR_STATE, "rk_profile_read / rk_profile_timeline must follow each profiled decode");
         c->prof_used = it->second.prof_events;
         c->prof_flops = it->second.prof_flops;
+        c->tl_meta = it->second.tl_marks;
     }
     cudaError_t e = cudaGraphLaunch(it->second.exec, c->stream);
     if (e != cudaSuccess) return fail_cuda_err(RK_ERR_LAUNCH, "graph launch", e);

@@ -160,6 +160,12 @@ struct StageRec {  // captured stage activations (rk_record_stages)
 
 }  // namespace rk
 
+// one timeline mark: the stream index and the launch name
+struct TlMarkRec {
+    int stream;
+    std::string name;
+};
+
 struct rk_ctx {
     int device = 0;
     int precision = RK_PRECISION_FP32;
@@ -195,6 +201,7 @@ struct rk_ctx {
         long long launches = 0;
         size_t prof_events = 0;
         std::vector<double> prof_flops;
+        std::vector<struct TlMarkRec> tl_marks;
     };
     std::map<std::pair<int, int>, GraphRec> graphs;
     // profiling (rk_profile): mode bits RK_PROFILE_*; event pairs around each conv launch
@@ -203,7 +210,7 @@ struct rk_ctx {
     // timeline (RK_PROFILE_TIMELINE): one event after every launch, with its stream and name;
     // event 0 of a decode is the "start" mark on the context stream
     std::vector<cudaEvent_t> tl_events;
-    struct TlMark { int stream; std::string name; };
+    using TlMark = TlMarkRec;
     std::vector<TlMark> tl_meta;
     std::vector<cudaEvent_t> prof_events;  // pool, 2 per launch
     size_t prof_used = 0;

@@ -75,7 +75,8 @@ extern "C" rk_status rk_create(int device, const rk_options* opts, rk_ctx** out)
               cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&c->rb[0], cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&c->rb[1], cudaStreamNonBlocking) == cudaSuccess;
-    cudaEvent_t* evs[] = {&c->ev_fork, &c->ev_join, &c->ev_src[0], &c->ev_src[1], &c->ev_u, &c->ev_rb[0], &c->ev_rb[1]};
+    cudaEvent_t* evs[] = {&c->ev_fork, &c->ev_join, &c->ev_src[0], &c->ev_src[1], &c->ev_u, &c->ev_rb[0], &c->ev_rb[1],
+                          &c->ev_sc[0], &c->ev_sc[1]};
     for (cudaEvent_t* e : evs) ok = ok && cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaMalloc(&c->err, 256) == cudaSuccess && cudaMemset(c->err, 0, 256) == cudaSuccess;
     if (!ok) {
@@ -100,7 +101,8 @@ extern "C" void rk_destroy(rk_ctx* c) {
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     for (cudaEvent_t e : c->tl_events) cudaEventDestroy(e);
     if (c->err) cudaFree(c->err);
-    cudaEvent_t evs[] = {c->ev_fork, c->ev_join, c->ev_src[0], c->ev_src[1], c->ev_u, c->ev_rb[0], c->ev_rb[1]};
+    cudaEvent_t evs[] = {c->ev_fork, c->ev_join, c->ev_src[0], c->ev_src[1], c->ev_u, c->ev_rb[0], c->ev_rb[1],
+                         c->ev_sc[0], c->ev_sc[1]};
     for (cudaEvent_t e : evs)
         if (e) cudaEventDestroy(e);
     for (cudaStream_t s : c->rb)

@@ -185,6 +185,26 @@ void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* 
     Lane& ln = w.lane[0];
     const int To = b.upsample ? 2 * T : T;
     const bool sp = r.split;
+    // shortcut: 1x1 conv at T rows (nearest upsample commutes with it), on
+    // resblock lane 1 beside the main branch (it only needs x); joined before conv2
+    const float* res = x;
+    int ldres = ldx, shift = 0;
+    const bool serial = r.c->profile && (r.c->prof_mode & RK_PROFILE_SERIAL);
+    Run rs{r.c, serial ? r.st : r.c->rb[0], sp};
+    if (b.shortcut) {
+        if (!r.ok()) return;
+        if (rs.st != r.st && (cudaEventRecord(r.c->ev_sc[0], r.st) != cudaSuccess ||
+                              cudaStreamWaitEvent(rs.st, r.c->ev_sc[0], 0) != cudaSuccess)) {
+            r.status = fail_cuda(RK_ERR_CUDA, "shortcut fork");
+            return;
+        }
+        pack(rs, x, ldx, T, b.din, w.op_b, b.conv1x1.Cp, sp);
+        ConvCall cs;
+        cs.w = &b.conv1x1; cs.op = &w.op_b; cs.rows_in = T; cs.split = sp; cs.M = T; cs.T_out = T;
+        cs.y = w.enc_sc; cs.ldy = b.dout; cs.use_bias = false;
+        conv(rs, cs);
+        res = w.enc_sc; ldres = b.dout; shift = b.upsample ? 1 : 0;
+    }
     // norm1 -> LeakyReLU(0.2) [-> depthwise ConvTranspose upsample] -> operand
     coef(r, stats_x, parts_x, ldsx, 0, b.norm1, T, fc, ln);
     if (b.upsample) {
@@ -201,16 +221,12 @@ void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* 
     conv(r, c1);
     coef(r, ln.stats_a, stats_parts_for(c1), b.dout, 0, b.norm2, To, fc, ln);
     pack(r, w.enc_r1, b.dout, To, b.dout, ln.op, b.conv2.Cp, sp, ln.coef, nullptr, 0.2f, true);
-    // shortcut: 1x1 conv at T rows (nearest upsample commutes with it)
-    const float* res = x;
-    int ldres = ldx, shift = 0;
     if (b.shortcut) {
-        pack(r, x, ldx, T, b.din, w.op_b, b.conv1x1.Cp, sp);
-        ConvCall cs;
-        cs.w = &b.conv1x1; cs.op = &w.op_b; cs.rows_in = T; cs.split = sp; cs.M = T; cs.T_out = T;
-        cs.y = w.enc_sc; cs.ldy = b.dout; cs.use_bias = false;
-        conv(r, cs);
-        res = w.enc_sc; ldres = b.dout; shift = b.upsample ? 1 : 0;
+        r.merge(rs);
+        if (rs.st != r.st && r.ok() &&
+            (cudaEventRecord(r.c->ev_sc[1], rs.st) != cudaSuccess ||
+             cudaStreamWaitEvent(r.st, r.c->ev_sc[1], 0) != cudaSuccess))
+            r.status = fail_cuda(RK_ERR_CUDA, "shortcut join");
     }
     // conv2 + shortcut + bias, times 1/sqrt(2)
     ConvCall c2;

@@ -178,6 +178,8 @@ struct rk_ctx {
     // done), u (main -> resblock lanes), rb[j] (resblock lane j -> main)
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr, ev_src[2] = {nullptr, nullptr}, ev_u = nullptr,
                 ev_rb[2] = {nullptr, nullptr};
+    // AdainResBlk1d shortcut branch fork / join (main <-> resblock lane 1)
+    cudaEvent_t ev_sc[2] = {nullptr, nullptr};
     bool use_graphs = true;
     uint32_t* err = nullptr;      // device error word
     // split-K scratch of the conv launcher, one per stream (main, side, rb[0], rb[1]):

@@ -197,31 +197,49 @@ __global__ void dw_upsample_pack_kernel(const float* __restrict__ x, int ldx, in
     }
 }
 
-// One thread per harmonic; the cumulative sum runs serially in the same float
-// order as the reference (src/kernels.cu:1352-1383).
-__global__ void sinegen_phase_kernel(const float* __restrict__ f0, int L2, const float* __restrict__ rand_ini,
-                                     float* __restrict__ phase_low) {
-    const int h = threadIdx.x;
-    if (h >= 9) return;
+// Per-frame phase increments of the 9 harmonics (src/kernels.cu:1337-1384):
+// the increments of a chunk of frames are computed by the whole block (they do
+// not depend on one another) and staged in shared memory; one thread per
+// harmonic then runs the cumulative sum serially, in the reference's order, so
+// the phase is bit-identical to a one-thread scan.
+__global__ void __launch_bounds__(1024) sinegen_phase_kernel(const float* __restrict__ f0, int L2,
+                                                             const float* __restrict__ rand_ini,
+                                                             float* __restrict__ phase_low) {
+    constexpr int CH = 1024;  // frames per chunk
+    __shared__ float vs[9][CH];
     const int T_audio = L2 * 300;
-    const float ri = rand_ini[h];
-    float run = 0.f;
     const float scale = __fmul_rn(__fmul_rn(2.0f, 3.14159265358979323846f), 300.0f);
-    for (int t = 0; t < L2; t++) {
-        float src = __fsub_rn(__fdiv_rn(__fmul_rn(__fadd_rn((float)t, 0.5f), (float)T_audio), (float)L2), 0.5f);
-        src = fmaxf(0.0f, fminf(src, (float)(T_audio - 1)));
-        const int lo = (int)src;
-        const int hi = min(lo + 1, T_audio - 1);
-        const float frac = __fsub_rn(src, (float)lo);
-        float rad_lo = fmodf(__fdiv_rn(__fmul_rn(f0[lo / 300], (float)(h + 1)), 24000.0f), 1.0f);
-        float rad_hi = fmodf(__fdiv_rn(__fmul_rn(f0[hi / 300], (float)(h + 1)), 24000.0f), 1.0f);
-        if (rad_lo < 0.0f) rad_lo = __fadd_rn(rad_lo, 1.0f);
-        if (rad_hi < 0.0f) rad_hi = __fadd_rn(rad_hi, 1.0f);
-        if (lo == 0) rad_lo = __fadd_rn(rad_lo, ri);
-        if (hi == 0) rad_hi = __fadd_rn(rad_hi, ri);
-        const float v = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, frac), rad_lo), __fmul_rn(frac, rad_hi));
-        run = t == 0 ? v : __fadd_rn(run, v);
-        phase_low[t * 9 + h] = __fmul_rn(run, scale);
+    float run = 0.f;  // carried across chunks by threads 0..8
+    for (int t0 = 0; t0 < L2; t0 += CH) {
+        const int n = min(CH, L2 - t0);
+        for (int i = threadIdx.x; i < 9 * n; i += blockDim.x) {
+            const int h = i / n, tt = i - h * n;
+            const int t = t0 + tt;
+            const float ri = rand_ini[h];
+            float src = __fsub_rn(__fdiv_rn(__fmul_rn(__fadd_rn((float)t, 0.5f), (float)T_audio), (float)L2), 0.5f);
+            src = fmaxf(0.0f, fminf(src, (float)(T_audio - 1)));
+            const int lo = (int)src;
+            const int hi = min(lo + 1, T_audio - 1);
+            const float frac = __fsub_rn(src, (float)lo);
+            float rad_lo = fmodf(__fdiv_rn(__fmul_rn(f0[lo / 300], (float)(h + 1)), 24000.0f), 1.0f);
+            float rad_hi = fmodf(__fdiv_rn(__fmul_rn(f0[hi / 300], (float)(h + 1)), 24000.0f), 1.0f);
+            if (rad_lo < 0.0f) rad_lo = __fadd_rn(rad_lo, 1.0f);
+            if (rad_hi < 0.0f) rad_hi = __fadd_rn(rad_hi, 1.0f);
+            if (lo == 0) rad_lo = __fadd_rn(rad_lo, ri);
+            if (hi == 0) rad_hi = __fadd_rn(rad_hi, ri);
+            vs[h][tt] = __fadd_rn(__fmul_rn(__fsub_rn(1.0f, frac), rad_lo), __fmul_rn(frac, rad_hi));
+        }
+        __syncthreads();
+        if (threadIdx.x < 9) {
+            const int h = threadIdx.x;
+#pragma unroll 8
+            for (int tt = 0; tt < n; tt++) {
+                const int t = t0 + tt;
+                run = t == 0 ? vs[h][tt] : __fadd_rn(run, vs[h][tt]);
+                phase_low[t * 9 + h] = __fmul_rn(run, scale);
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -388,7 +406,7 @@ int cur_dev() {
 }
 
 void sinegen_phase(const float* f0, int L2, float* phase_low, cudaStream_t st) {
-    sinegen_phase_kernel<<<1, 32, 0, st>>>(f0, L2, g_rand_ini_ptr[cur_dev()], phase_low);
+    sinegen_phase_kernel<<<1, 1024, 0, st>>>(f0, L2, g_rand_ini_ptr[cur_dev()], phase_low);
 }
 
 void sinegen_source(const float* phase_low, const float* f0, const float* lw, const float* lb, float* out, int L2,

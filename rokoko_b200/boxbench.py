@@ -1,0 +1,161 @@
+"""Box throughput over many utterances, one process per GPU.
+
+    python -m rokoko_b200.boxbench [--count 1024] [--batch 32] [--fp32]
+    python -m torch.distributed.run --nproc-per-node N -m rokoko_b200.boxbench ...
+
+Workload: `count` utterances with token counts from a seeded truncated normal
+(mean 120, sd 60, clipped to [16, 510]), durations U[2, 8], a seeded style
+vector each (configs.config4), FP16 weights (the KOKO v2 file) unless --fp32.
+The utterances are sharded over the ranks by rokoko_b200.shard (length
+buckets, greedy longest-processing-time; no collective in the data path);
+each rank runs its share through rk_encode + rk_decode in batches of `batch`
+utterances in the plan's bucket order, dealt round-robin to `contexts` rk_ctx
+on the same GPU, each driven by its own host thread, so that one context's
+latency-bound front half (ALBERT, BiLSTM recurrences) overlaps another's
+SM-saturating decode; rank 0 gathers the PCM on the host.
+
+Reported (rank 0, one JSON line): total audio seconds / wall time from the
+first dispatch to the last PCM gathered, the per-rank maximum wall time, the
+load imbalance of the shard plan and the front-half / decode split of rank 0.
+Before the timed pass every rank runs one utterance of each decode-length
+bucket of its share, so the timed pass replays cached decode graphs.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+import threading
+import time
+
+import numpy as np
+
+
+def _args(argv=None):
+    p = argparse.ArgumentParser(prog="rokoko_b200.boxbench")
+    p.add_argument("--count", type=int, default=1024)
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--fp32", action="store_true")
+    p.add_argument("--contexts", type=int, default=2,
+                   help="rk_ctx per GPU, each driven by its own host thread on alternating batches")
+    return p.parse_args(argv)
+
+
+def main(argv=None) -> int:
+    a = _args(argv)
+    import torch
+    import torch.distributed as dist
+
+    from . import configs, convert_v2, koko, shard
+    from .context import FP16, FP32, Context
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        # host-side process group: barriers and the PCM gather move bytes on the host
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+
+    utts = configs.config4(seed=a.seed, count=a.count)
+    items = shard.units(utts)
+    assignment = shard.plan(items, world)
+    mine = assignment[rank]
+
+    blob = koko.random_v1_blob(0)
+    prec = FP32 if a.fp32 else FP16
+    if prec == FP16:
+        blob = convert_v2.convert_blob(blob)
+    ctxs = [Context(local, prec) for _ in range(max(1, a.contexts))]
+    for ctx in ctxs:
+        ctx.load_weights(blob)
+
+    # batches of this rank's share (plan order), dealt round-robin to the contexts
+    batches = [mine[k:k + a.batch] for k in range(0, len(mine), a.batch)]
+    per_ctx = [batches[c::len(ctxs)] for c in range(len(ctxs))]
+
+    # warm-up outside the timed pass: one utterance of every decode-length bucket
+    # each context will see (the decode graphs are cached per bucket), largest
+    # first so that the decode workspace is sized once
+    for ctx, bl in zip(ctxs, per_ctx):
+        first = {}
+        for b in bl:
+            for i in b:
+                first.setdefault(items[i].L_b, i)
+        warm = [first[k] for k in sorted(first, reverse=True)]
+        for k in range(0, len(warm), a.batch):
+            _, Ls = ctx.encode([utts[i] for i in warm[k:k + a.batch]])
+            ctx.decode(Ls)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # one host thread per context: while one context runs the latency-bound front
+    # half (encode) of a batch, another's decoders fill the SMs
+    results = [[] for _ in ctxs]
+    timings = [[0.0, 0.0] for _ in ctxs]
+    errors = []
+
+    def worker(c: int) -> None:
+        try:
+            for idx in per_ctx[c]:
+                te = time.perf_counter()
+                _, Ls = ctxs[c].encode([utts[i] for i in idx])
+                td = time.perf_counter()
+                pcms = ctxs[c].decode(Ls)
+                timings[c][0] += td - te
+                timings[c][1] += time.perf_counter() - td
+                results[c].extend(zip(idx, pcms))
+        except BaseException as e:  # re-raised after the join
+            errors.append(e)
+
+    t0 = time.perf_counter()
+    threads = [threading.Thread(target=worker, args=(c,)) for c in range(len(ctxs))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    if errors:
+        raise errors[0]
+    local_pcm = [x for r in results for x in r]
+    t_enc = sum(t[0] for t in timings)
+    t_dec = sum(t[1] for t in timings)
+    t_rank = time.perf_counter() - t0
+    out = shard.gather_pcm(local_pcm, len(utts))
+    t_all = time.perf_counter() - t0
+    t_max = t_rank
+    if world > 1:
+        tt = torch.tensor([t_rank], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max = float(tt.item())
+
+    if rank == 0:
+        samples = sum(p.shape[0] for p in out)
+        expected = sum(600 * int(np.asarray(u.durations).sum()) for u in utts)
+        audio_s = samples / 24000.0
+        line = {
+            "metric": "box throughput, audio-sec/sec", "value": round(audio_s / t_all, 2), "unit": "audio-s/s",
+            "n_gpus": world, "utterances": len(utts), "audio_s": round(audio_s, 1),
+            "samples_match_durations": samples == expected,
+            "wall_s": round(t_all, 3), "max_rank_s": round(t_max, 3),
+            "plan_imbalance": round(shard.imbalance(items, assignment), 4),
+            "rank0": {"utterances": len(mine), "contexts": len(ctxs), "encode_s_summed": round(t_enc, 3),
+                      "decode_s_summed": round(t_dec, 3)},
+            "precision": "FP32 semantics (split bf16)" if a.fp32 else "FP16 weights (KOKO v2), FP32 accumulate",
+            "config": "config4: T ~ truncated N(120, 60) in [16, 510] + BOS/EOS, durations U[2,8], seeded styles",
+            "batch": a.batch, "data": "synthetic; random-init weights",
+        }
+        print(json.dumps(line), flush=True)
+    for ctx in ctxs:
+        ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -25,3 +25,44 @@ def test_encode_decode_batch_matches_single_utterance_infer(v1_blob):
             assert np.array_equal(pcm, ref)
         # nothing pending after rk_decode
         assert ctx.decode([]) == []
+
+
+def test_two_contexts_on_two_threads_match_one_context(v1_blob):
+    """Two rk_ctx on one GPU, each driven by its own host thread at the same
+    time (the box-throughput setup of rokoko_b200.boxbench), produce PCM
+    bit-identical to one context running the same batches alone."""
+    import threading
+
+    from rokoko_b200 import configs
+    from rokoko_b200.context import FP32, Context
+    batches = [[configs.config0(seed=10 + 3 * b + k, n_phon=6 + 5 * k) for k in range(3)] for b in range(4)]
+    with Context(0, FP32) as ctx:
+        ctx.load_weights(v1_blob)
+        ref = [ctx.decode(ctx.encode(bt)[1]) for bt in batches]
+    ctxs = [Context(0, FP32), Context(0, FP32)]
+    try:
+        for c in ctxs:
+            c.load_weights(v1_blob)
+        out = [None] * len(batches)
+        errors = []
+
+        def worker(c):
+            try:
+                for b in range(c, len(batches), 2):
+                    out[b] = ctxs[c].decode(ctxs[c].encode(batches[b])[1])
+            except BaseException as e:
+                errors.append(e)
+
+        th = [threading.Thread(target=worker, args=(c,)) for c in range(2)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert not errors, errors
+        for b in range(len(batches)):
+            assert len(out[b]) == len(ref[b])
+            for p, r in zip(out[b], ref[b]):
+                assert np.array_equal(p, r)
+    finally:
+        for c in ctxs:
+            c.close()

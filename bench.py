@@ -14,8 +14,10 @@ weak scaling).  Metric: audio-seconds per second over all GPUs.
 inputs resident in HBM; L2 is flushed (256 MB write) before every timed step,
 outside the events.  `e2e` is the same metric through the host-buffer C-ABI
 call rk_decode_features (pinned host inputs, host PCM out) timed with the
-wall clock.  `roofline` is the tcgen05 conv kernel measured live with CUDA
-events around every launch of the timed region.  Under torchrun each rank
+wall clock.  `roofline` is the tcgen05 conv kernel measured live on a second
+pass of the same steps, replayed as a profiling CUDA graph with every lane on
+one stream, each conv launch bracketed by its own event nodes (the kernels'
+own time).  Under torchrun each rank
 drives LOCAL_RANK's GPU; ranks meet at a barrier and the max over ranks is
 reported by rank 0.
 """

@@ -359,15 +359,17 @@ __global__ void __launch_bounds__(320, 1)
     }
 }
 
-// Split-K second stage: one block per (128 channels, 64-row part); thread
-// (x, y) owns channel x and rows y*8 .. y*8+7 of the part.  Sums the k_split
+// Split-K second stage: one block per (32 channels, 64-row part); thread
+// (x, y) owns channel x and rows y*8 .. y*8+7 of the part.  256-thread blocks
+// leave room for every row's and slice's load in flight at once.  Sums the k_split
 // raw accumulators in slice order, applies the same epilogue as the conv kernel
 // (residual, bias, activation, accumulator input, scale, reflection-pad
 // duplicate) and writes the part's statistics, combined over y in a fixed order.
-__global__ void __launch_bounds__(1024) splitk_reduce_kernel(const __grid_constant__ ConvArgs a, int n_phases) {
-    __shared__ float red_s[8][128], red_q[8][128];
+template <int KS>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const __grid_constant__ ConvArgs a, int n_phases) {
+    __shared__ float red_s[8][32], red_q[8][32];
     const int cx = threadIdx.x, ry = threadIdx.y;
-    const int co = blockIdx.x * 128 + cx;
+    const int co = blockIdx.x * 32 + cx;
     const int ppp = (a.M + STATS_ROWS - 1) / STATS_ROWS;
     const int phase = blockIdx.y / ppp, p = blockIdx.y - phase * ppp;
     const bool co_ok = co < a.C_out;
@@ -375,23 +377,24 @@ __global__ void __launch_bounds__(1024) splitk_reduce_kernel(const __grid_consta
     const float bias_v = (a.bias && co_ok) ? a.bias[co] : 0.0f;
     float s = 0.f, q = 0.f;
     const int m0 = p * STATS_ROWS + ry * 8;
+    // every row's and slice's load in flight before the ordered sums: addresses are
+    // clamped into the slice (rows past M and channels past C_out are discarded below)
+    const int co_c = co_ok ? co : a.C_out - 1;
+    float pv[KS][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int m_c = m0 + i < a.M ? m0 + i : a.M - 1;
+        const float* src = a.part_out + ((size_t)phase * a.M + m_c) * a.C_out + co_c;
+#pragma unroll
+        for (int k = 0; k < KS; k++) pv[k][i] = src[k * slice];
+    }
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const int m = m0 + i;
-        v[i] = 0.f;
-        if (co_ok && m < a.M) {
-            // every slice's load in flight before the ordered sum
-            const float* src = a.part_out + ((size_t)phase * a.M + m) * a.C_out + co;
-            float pv[MAX_K_SPLIT];
+        float acc = pv[0][i];
 #pragma unroll
-            for (int k = 0; k < MAX_K_SPLIT; k++) pv[k] = k < a.k_split ? src[k * slice] : 0.f;
-            float acc = pv[0];
-#pragma unroll
-            for (int k = 1; k < MAX_K_SPLIT; k++)
-                if (k < a.k_split) acc += pv[k];
-            v[i] = acc;
-        }
+        for (int k = 1; k < KS; k++) acc += pv[k][i];
+        v[i] = acc;
     }
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -495,8 +498,17 @@ cudaError_t launch_inst(const ConvOperands& ops, ConvArgs a, int halo, int n_pha
     cudaError_t e = cudaGetLastError();
     if (kernels) *kernels = ks > 1 ? 2 : 1;
     if (e != cudaSuccess || ks == 1) return e;
-    dim3 rg((a.C_out + 127) / 128, conv_tc_stats_parts(a.M, n_phases));
-    splitk_reduce_kernel<<<rg, dim3(128, 8), 0, stream>>>(a, n_phases);
+    dim3 rg((a.C_out + 31) / 32, conv_tc_stats_parts(a.M, n_phases));
+    const dim3 rb(32, 8);
+    switch (ks) {
+        case 2: splitk_reduce_kernel<2><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        case 3: splitk_reduce_kernel<3><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        case 4: splitk_reduce_kernel<4><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        case 5: splitk_reduce_kernel<5><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        case 6: splitk_reduce_kernel<6><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        case 7: splitk_reduce_kernel<7><<<rg, rb, 0, stream>>>(a, n_phases); break;
+        default: splitk_reduce_kernel<MAX_K_SPLIT><<<rg, rb, 0, stream>>>(a, n_phases); break;
+    }
     return cudaGetLastError();
 }
 

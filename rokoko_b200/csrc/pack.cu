@@ -81,23 +81,46 @@ __global__ void pack_act_kernel(PackArgs a) {
     }
 }
 
-// Fast path: plain rows (no super-row gather), C a multiple of 8.  One thread
-// = 8 channels of one row: two float4 loads, one 16-byte store per plane.
+// Fast path: plain rows (no super-row gather), C a multiple of 8, every
+// per-channel table 16-byte aligned, fewer than 2^31 groups.  One thread = 8
+// channels of one row: two float4 loads of the row and of each per-channel
+// table, one 16-byte store per plane.
+__device__ __forceinline__ void load8(const float* p, int c, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p + c)[0], b = reinterpret_cast<const float4*>(p + c)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 template <bool SPLIT>
 __global__ void pack_act_vec_kernel(PackArgs a) {
     const int groups = a.Cp >> 3, cgroups = a.C >> 3;
-    const long total = (long)a.rows_dst * groups;
-    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
-        const int q = (int)(idx / groups);
-        const int g = (int)(idx - (long)q * groups);
+    const int total = a.rows_dst * groups;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const int q = idx / groups;
+        const int g = idx - q * groups;
         float v[8];
         if (g < cgroups && q < a.rows_src) {
-            const float4* src = reinterpret_cast<const float4*>(a.x + (long)q * a.ldx + g * 8);
-            const float4 p0 = src[0], p1 = src[1];
-            v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
-            v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+            load8(a.x + (size_t)q * a.ldx, g * 8, v);
+            if (a.scale) {
+                float sc[8], sh[8];
+                load8(a.scale, g * 8, sc);
+                load8(a.shift, g * 8, sh);
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = act_transform(v[j], g * 8 + j, a);
+                for (int j = 0; j < 8; j++) v[j] = sc[j] * v[j] + sh[j];
+            }
+            if (a.snake) {
+                float al[8];
+                load8(a.snake, g * 8, al);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float sn = snake_sin(al[j] * v[j]);
+                    v[j] = v[j] + sn * sn * (1.0f / al[j]);
+                }
+            }
+            if (a.lrelu) {
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = v[j] > 0.0f ? v[j] : a.slope * v[j];
+            }
         } else {
 #pragma unroll
             for (int j = 0; j < 8; j++) v[j] = 0.0f;
@@ -196,8 +219,9 @@ cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
     if ((a.Cp & 63) || a.sr_stride < 1) return cudaErrorInvalidValue;
     const long total = (long)a.rows_dst * (a.Cp >> 3);
     if (total == 0) return cudaSuccess;
-    const bool vec = a.sr_stride == 1 && a.sr_pad == 0 && (a.C & 7) == 0 && (a.ldx & 3) == 0 &&
-                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+    auto al16 = [](const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool vec = a.sr_stride == 1 && a.sr_pad == 0 && (a.C & 7) == 0 && (a.ldx & 3) == 0 && al16(a.x) &&
+                     al16(a.scale) && al16(a.shift) && al16(a.snake) && total < (1L << 31) - 148L * 16 * 256;
     if (vec) {
         if (split) pack_act_vec_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
         else pack_act_vec_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);

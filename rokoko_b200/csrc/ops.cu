@@ -34,6 +34,9 @@ int nblocks(long work, int threads, int cap = 148 * 16) {
     return (int)(b < 1 ? 1 : b);
 }
 
+// element counts for which a 32-bit grid-stride index cannot overflow
+bool small_index(long total) { return total < (1L << 31) - 148L * 16 * 1024; }
+
 __global__ void style_fc_kernel(const float* __restrict__ W, const float* __restrict__ b,
                                 const float* __restrict__ s, float* __restrict__ out, int rows) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -47,13 +50,12 @@ __global__ void style_fc_kernel(const float* __restrict__ W, const float* __rest
     if (lane == 0) out[warp] = acc + b[warp];
 }
 
-// block = 32 channels x 32 part-lanes; each lane sums a strided subset of the
-// parts (fixed order), then the 32 lanes are combined in a fixed tree.
 // AdaIN coefficients from the InstanceNorm partials: block = 8 channels x 128
-// part slices; slice y sums parts y, y + 128, ... in double (loads in flight
-// together), then a fixed-order halving tree over the slices.  mean = S / T,
-// var = Q / T - mean^2 (biased, the reference's single-pass form), scale =
-// (1 + gamma) w / sqrt(var + 1e-5), shift = (1 + gamma)(b - w mean / sqrt(var + eps)) + beta.
+// part slices; slice y sums parts y, y + 128, ... in double (eight loads of
+// each kind in flight together), then a fixed-order halving tree over the
+// slices.  mean = S / T, var = Q / T - mean^2 (biased, the reference's
+// single-pass form), scale = (1 + gamma) w / sqrt(var + 1e-5),
+// shift = (1 + gamma)(b - w mean / sqrt(var + eps)) + beta.
 __global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restrict__ stats, int parts, int ld,
                                                           int col0, int C, int T, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta,
@@ -64,20 +66,22 @@ __global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restric
     const int c = blockIdx.x * 8 + cx;
     double s = 0.0, q = 0.0;
     if (c < C) {
-        int p = py;
-        for (; p + 384 < parts; p += 512) {
-            const float s0 = stats[(size_t)p * ld + col0 + c], s1 = stats[(size_t)(p + 128) * ld + col0 + c];
-            const float s2 = stats[(size_t)(p + 256) * ld + col0 + c], s3 = stats[(size_t)(p + 384) * ld + col0 + c];
-            const float q0 = stats[(size_t)(parts + p) * ld + col0 + c];
-            const float q1 = stats[(size_t)(parts + p + 128) * ld + col0 + c];
-            const float q2 = stats[(size_t)(parts + p + 256) * ld + col0 + c];
-            const float q3 = stats[(size_t)(parts + p + 384) * ld + col0 + c];
-            s += s0; s += s1; s += s2; s += s3;
-            q += q0; q += q1; q += q2; q += q3;
-        }
-        for (; p < parts; p += 128) {
-            s += stats[(size_t)p * ld + col0 + c];
-            q += stats[(size_t)(parts + p) * ld + col0 + c];
+        // eight parts per slice in flight at once: addresses clamped to the last
+        // part, the sums predicated (parts ascending, as a serial loop would add them)
+        for (int p0 = py; p0 < parts; p0 += 8 * 128) {
+            float sv[8], qv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int pc = min(p0 + u * 128, parts - 1);
+                sv[u] = stats[(size_t)pc * ld + col0 + c];
+                qv[u] = stats[(size_t)(parts + pc) * ld + col0 + c];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (p0 + u * 128 < parts) {
+                    s += sv[u];
+                    q += qv[u];
+                }
         }
     }
     sh_s[py][cx] = s;
@@ -150,12 +154,15 @@ __global__ void f0n_down_kernel(const float* __restrict__ f0, const float* __res
     nd[t] = b + bn[0];
 }
 
+// I = int when the element count leaves room for the grid stride below 2^31
+// (32-bit division), long otherwise.
+template <typename I>
 __global__ void concat_cols_kernel(float* dst, int ld, int col0, int T, const float* a, int lda, int ca,
                                    const float* b, int ldb, int cb, const float* c, const float* d) {
     const int W = ca + cb + (c ? 1 : 0) + (d ? 1 : 0);
-    const long total = (long)T * W;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / W), j = (int)(i - (long)t * W);
+    const I total = (I)T * W;
+    for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+        const int t = (int)(i / W), j = (int)(i - (I)t * W);
         float v;
         if (j < ca) v = a[(size_t)t * lda + j];
         else if (j < ca + cb) v = b[(size_t)t * ldb + (j - ca)];
@@ -165,15 +172,15 @@ __global__ void concat_cols_kernel(float* dst, int ld, int col0, int T, const fl
     }
 }
 
-template <bool SPLIT>
+template <bool SPLIT, typename I>
 __global__ void dw_upsample_pack_kernel(const float* __restrict__ x, int ldx, int T, int C,
                                         const float* __restrict__ scale, const float* __restrict__ shift,
                                         float slope, const float* __restrict__ w, const float* __restrict__ bias,
                                         void* hi, void* lo, int Cp) {
     const int To = 2 * T;
-    const long total = (long)To * Cp;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / Cp), c = (int)(i - (long)t * Cp);
+    const I total = (I)To * Cp;
+    for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+        const int t = (int)(i / Cp), c = (int)(i - (I)t * Cp);
         float v = 0.f;
         if (c < C) {
             float acc = 0.f;
@@ -380,18 +387,23 @@ void f0n_down(const float* f0, const float* n, const float* wf, const float* bf,
 void concat_cols(float* dst, int ld, int col0, int T, const float* a, int lda, int ca, const float* b, int ldb,
                  int cb, const float* c, const float* d, cudaStream_t st) {
     const long total = (long)T * (ca + cb + 2);
-    concat_cols_kernel<<<nblocks(total, 256), 256, 0, st>>>(dst, ld, col0, T, a, lda, ca, b, ldb, cb, c, d);
+    if (small_index(total))
+        concat_cols_kernel<int><<<nblocks(total, 256), 256, 0, st>>>(dst, ld, col0, T, a, lda, ca, b, ldb, cb, c, d);
+    else
+        concat_cols_kernel<long><<<nblocks(total, 256), 256, 0, st>>>(dst, ld, col0, T, a, lda, ca, b, ldb, cb, c, d);
 }
 
 void dw_upsample_pack(const float* x, int ldx, int T, int C, const float* scale, const float* shift, float slope,
                       const float* w, const float* b, void* hi, void* lo, int Cp, bool split, cudaStream_t st) {
     const long total = (long)2 * T * Cp;
-    if (split)
-        dw_upsample_pack_kernel<true><<<nblocks(total, 256), 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b,
-                                                                           hi, lo, Cp);
-    else
-        dw_upsample_pack_kernel<false><<<nblocks(total, 256), 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w,
-                                                                            b, hi, lo, Cp);
+    const int g = nblocks(total, 256);
+    if (small_index(total)) {
+        if (split) dw_upsample_pack_kernel<true, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+        else dw_upsample_pack_kernel<false, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+    } else {
+        if (split) dw_upsample_pack_kernel<true, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+        else dw_upsample_pack_kernel<false, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+    }
 }
 
 namespace {

@@ -43,13 +43,14 @@ __device__ __forceinline__ float act_transform(float v, int c, const PackArgs& a
 }
 
 // one thread = 8 consecutive destination channels of one destination row
-template <bool SPLIT>
+// I = int when the group count leaves room for the grid stride below 2^31.
+template <bool SPLIT, typename I>
 __global__ void pack_act_kernel(PackArgs a) {
     const int groups = a.Cp >> 3;
-    const long total = (long)a.rows_dst * groups;
-    for (long idx = (long)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+    const I total = (I)a.rows_dst * groups;
+    for (I idx = (I)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (I)gridDim.x * blockDim.x) {
         const int q = (int)(idx / groups);
-        const int g = (int)(idx - (long)q * groups);
+        const int g = (int)(idx - (I)q * groups);
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -207,6 +208,55 @@ __global__ void pack_avg3_kernel(const float* __restrict__ x0, const float* __re
     }
 }
 
+// pack_avg3 fast path: C a multiple of 8, every tensor 16-byte aligned, fewer
+// than 2^31 groups; float4 loads and stores, 32-bit indexing.
+template <bool SPLIT>
+__global__ void pack_avg3_vec_kernel(const float* __restrict__ x0, const float* __restrict__ x1,
+                                     const float* __restrict__ x2, int T, int C, int Cp, float slope, void* hi,
+                                     void* lo, float* f32_out) {
+    const int groups = Cp >> 3, cgroups = C >> 3;
+    const int total = T * groups;
+    const float third = 1.0f / 3.0f;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const int t = idx / groups;
+        const int g = idx - t * groups;
+        float v[8];
+        if (g < cgroups) {
+            const size_t o = (size_t)t * C + g * 8;
+            float a0[8], a1[8], a2[8];
+            load8(x0 + o, 0, a0);
+            load8(x1 + o, 0, a1);
+            load8(x2 + o, 0, a2);
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = ((a0[j] + a1[j]) + a2[j]) * third;
+            if (f32_out) {
+                reinterpret_cast<float4*>(f32_out + o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+                reinterpret_cast<float4*>(f32_out + o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = v[j] > 0.f ? v[j] : slope * v[j];
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.0f;
+        }
+        if (SPLIT) {
+            __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                h[j] = __float2bfloat16_rn(v[j]);
+                l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+            }
+            reinterpret_cast<uint4*>(hi)[idx] = *reinterpret_cast<uint4*>(h);
+            reinterpret_cast<uint4*>(lo)[idx] = *reinterpret_cast<uint4*>(l);
+        } else {
+            __align__(16) __half h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+            reinterpret_cast<uint4*>(hi)[idx] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+}
+
 int grid_for(long work, int threads) {
     long b = (work + threads - 1) / threads;
     if (b > 148L * 16) b = 148L * 16;
@@ -226,8 +276,11 @@ cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
         if (split) pack_act_vec_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
         else pack_act_vec_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
     } else {
-        if (split) pack_act_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(a);
-        else pack_act_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(a);
+        const bool small = total < (1L << 31) - 148L * 16 * 256;
+        if (split && small) pack_act_kernel<true, int><<<grid_for(total, 256), 256, 0, st>>>(a);
+        else if (split) pack_act_kernel<true, long><<<grid_for(total, 256), 256, 0, st>>>(a);
+        else if (small) pack_act_kernel<false, int><<<grid_for(total, 256), 256, 0, st>>>(a);
+        else pack_act_kernel<false, long><<<grid_for(total, 256), 256, 0, st>>>(a);
     }
     return cudaGetLastError();
 }
@@ -236,8 +289,16 @@ cudaError_t pack_avg3(const float* x0, const float* x1, const float* x2, int T, 
                       void* lo, bool split, float* f32_out, cudaStream_t st) {
     if (Cp & 63) return cudaErrorInvalidValue;
     const long total = (long)T * (Cp >> 3);
-    if (split) pack_avg3_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
-    else pack_avg3_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+    auto al16 = [](const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool vec = (C & 7) == 0 && al16(x0) && al16(x1) && al16(x2) && al16(f32_out) &&
+                     total < (1L << 31) - 148L * 16 * 256;
+    if (vec) {
+        if (split) pack_avg3_vec_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+        else pack_avg3_vec_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+    } else {
+        if (split) pack_avg3_kernel<true><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+        else pack_avg3_kernel<false><<<grid_for(total, 256), 256, 0, st>>>(x0, x1, x2, T, C, Cp, slope, hi, lo, f32_out);
+    }
     return cudaGetLastError();
 }
 

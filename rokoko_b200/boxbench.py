@@ -12,7 +12,8 @@ each rank runs its share through rk_encode + rk_decode in batches of `batch`
 utterances in the plan's bucket order, dealt round-robin to `contexts` rk_ctx
 on the same GPU, each driven by its own host thread, so that one context's
 latency-bound front half (ALBERT, BiLSTM recurrences) overlaps another's
-SM-saturating decode; rank 0 gathers the PCM on the host.
+SM-saturating decode; rank 0 gathers the PCM on the host (ranks on one host
+write it into one shared node-local file, rokoko_b200.shard.gather_pcm).
 
 Reported (rank 0, one JSON line): total audio seconds / wall time from the
 first dispatch to the last PCM gathered, the per-rank maximum wall time, the

@@ -14,14 +14,22 @@ PCM back in the original order.
   frame count (decoder FLOPs are linear in L) plus a per-token term for the
   front half; a bucket larger than a fair share is split so that one bucket
   cannot leave the other ranks idle.
-* Gather: with one process per GPU (torchrun) rank 0 collects every rank's
-  PCM over the host process group (gloo or the store; bytes on the host, not
-  a device collective); with one process and one host thread per GPU the
-  threads write into a shared list.
+* Gather: with one process per GPU (torchrun) the ranks exchange only
+  (utterance, sample count) over the host process group; when they share one
+  host, rank 0 maps one node-local file of the total size (/dev/shm) and every
+  rank writes its PCM at its utterances' offsets (original order), so the
+  samples cross no socket.  Ranks on different hosts fall back to a pickled
+  gather over the process group.  With one process and one host thread per
+  GPU the threads write into a shared list.  Nothing here is a device
+  collective.
 """
 from __future__ import annotations
 
+import os
+import socket
+import tempfile
 import threading
+import uuid
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
@@ -96,10 +104,16 @@ def run_rank(synth: Callable[[int], np.ndarray], indices: Sequence[int]) -> list
     return [(i, synth(i)) for i in indices]
 
 
+def _shm_dir() -> str:
+    return "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else tempfile.gettempdir()
+
+
 def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) -> list[np.ndarray] | None:
-    """Host-side gather of (index, PCM) pairs to rank 0 over torch.distributed
-    (gloo / the host store).  Returns the PCM list in original order on rank 0,
-    None elsewhere.  Without an initialised process group, returns `local` in order."""
+    """Gather of (index, PCM) pairs to rank 0 over the host process group.
+    Returns the PCM list in original order on rank 0, None elsewhere.  Ranks
+    on one host write into a shared node-local file (no sample crosses a
+    socket); otherwise the PCM is pickled through the group.  Without an
+    initialised process group, returns `local` in order."""
     import torch.distributed as dist
     if not (dist.is_available() and dist.is_initialized()):
         out: list = [None] * n_total
@@ -108,6 +122,17 @@ def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) ->
         return out
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    meta = [None] * world
+    dist.all_gather_object(meta, (socket.gethostname(), [(int(i), int(p.shape[0])) for i, p in local]), group=group)
+    lengths = [-1] * n_total
+    for _, part in meta:
+        for i, n in part:
+            lengths[i] = n
+    missing = [i for i, n in enumerate(lengths) if n < 0]
+    if missing:
+        raise RuntimeError(f"gather_pcm: no PCM for utterances {missing[:8]}")
+    if len({h for h, _ in meta}) == 1:
+        return _gather_shared_file(local, lengths, rank, group)
     bucket = [None] * world if rank == 0 else None
     dist.gather_object(local, bucket, dst=0, group=group)
     if rank != 0:
@@ -116,10 +141,42 @@ def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) ->
     for part in bucket:
         for i, pcm in part:
             out[i] = pcm
-    missing = [i for i, p in enumerate(out) if p is None]
-    if missing:
-        raise RuntimeError(f"gather_pcm: no PCM for utterances {missing[:8]}")
     return out
+
+
+def _gather_shared_file(local, lengths: list[int], rank: int, group) -> list[np.ndarray] | None:
+    """Node-local gather: rank 0 sizes a file for every sample (float32, original
+    order), each rank writes its own utterances at their offsets, rank 0 reads
+    the whole file back once and removes it."""
+    import torch.distributed as dist
+    offsets = np.zeros(len(lengths) + 1, np.int64)
+    np.cumsum(np.asarray(lengths, np.int64), out=offsets[1:])
+    total = int(offsets[-1])
+    name = [None]
+    if rank == 0:
+        name[0] = os.path.join(_shm_dir(), f"rk_pcm_{os.getpid()}_{uuid.uuid4().hex}")
+        with open(name[0], "wb") as f:
+            f.truncate(max(total, 1) * 4)
+    dist.broadcast_object_list(name, src=0, group=group)
+    path = name[0]
+    try:
+        if local and total:
+            mm = np.memmap(path, dtype=np.float32, mode="r+", shape=(total,))
+            for i, pcm in local:
+                mm[offsets[i]:offsets[i + 1]] = np.asarray(pcm, np.float32).reshape(-1)
+            mm.flush()
+            del mm
+        dist.barrier(group=group)
+        if rank != 0:
+            return None
+        flat = np.fromfile(path, dtype=np.float32, count=total) if total else np.zeros(0, np.float32)
+        return [flat[offsets[i]:offsets[i + 1]] for i in range(len(lengths))]
+    finally:
+        if rank == 0:
+            try:
+                os.remove(path)
+            except FileNotFoundError:
+                pass
 
 
 def run_threads(synths: Sequence[Callable[[int], np.ndarray]], items: Sequence[Unit]) -> list[np.ndarray]:

@@ -51,9 +51,12 @@ def _free_port():
     return p
 
 
-def _gloo_worker(rank, world, port, q):
+def _gloo_worker(rank, world, port, q, other_host=False):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if other_host and rank == 1:
+        # this rank claims another host: the gather must take the pickled path
+        shard.socket.gethostname = lambda: "another-host"
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
@@ -70,12 +73,13 @@ def _gloo_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_gather_pcm_over_gloo_world2():
+@pytest.mark.parametrize("other_host", [False, True], ids=["one-host-file", "two-hosts-pickled"])
+def test_gather_pcm_over_gloo_world2(other_host):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q, other_host)) for r in range(2)]
     for p in ps:
         p.start()
     res = [q.get(timeout=120) for _ in range(2)]

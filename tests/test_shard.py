@@ -51,7 +51,7 @@ def _free_port():
     return p
 
 
-def _gloo_worker(rank, world, port, q, other_host=False):
+def _gloo_worker(rank, world, port, q, other_host=False, n_utts=None):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if other_host and rank == 1:
@@ -60,7 +60,7 @@ def _gloo_worker(rank, world, port, q, other_host=False):
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        utts = configs.config2(seed=7)
+        utts = configs.config2(seed=7)[:n_utts]
         items = shard.units(utts)
         mine = shard.plan(items, world)[rank]
         local = shard.run_rank(lambda i: np.full(600 * items[i].L, i, np.float32), mine)
@@ -73,13 +73,14 @@ def _gloo_worker(rank, world, port, q, other_host=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("other_host", [False, True], ids=["one-host-file", "two-hosts-pickled"])
-def test_gather_pcm_over_gloo_world2(other_host):
+@pytest.mark.parametrize("other_host,n_utts", [(False, None), (True, None), (False, 1)],
+                         ids=["one-host-file", "two-hosts-pickled", "one-utterance-idle-rank"])
+def test_gather_pcm_over_gloo_world2(other_host, n_utts):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q, other_host)) for r in range(2)]
+    ps = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q, other_host, n_utts)) for r in range(2)]
     for p in ps:
         p.start()
     res = [q.get(timeout=120) for _ in range(2)]
@@ -88,5 +89,5 @@ def test_gather_pcm_over_gloo_world2(other_host):
         assert p.exitcode == 0
     got = [r for r in res if r is not None]
     assert len(got) == 1
-    items = shard.units(configs.config2(seed=7))
+    items = shard.units(configs.config2(seed=7)[:n_utts])
     assert got[0] == [(600 * u.L, float(u.index)) for u in items]

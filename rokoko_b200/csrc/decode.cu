@@ -238,8 +238,8 @@ void resblk1d(Run& r, const ResBlk1dW& b, const float* x, int ldx, const float* 
 }
 
 // AdaINResBlock1 (src/rokoko.cpp:775-801) on lane `ln`: x0 [T][C] with
-// partials sx0 (parts0 parts); rounds 0, 1 write ln.xa / ln.xb (with
-// partials), round 2 writes `out`.
+// partials sx0 (parts0 parts); dilation steps 0 and 1 (d = 1, 3) write
+// ln.xa / ln.xb (with partials), step 2 (d = 5) writes `out`.
 void resblock1(Run& r, Lane& ln, const ResBlock1W& rb, const float* x0, const float* sx0, int parts0, int T,
                float* out, const StyleFC& fc) {
     const int C = rb.C, K = rb.K;

@@ -146,8 +146,9 @@ def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) ->
 
 def _gather_shared_file(local, lengths: list[int], rank: int, group) -> list[np.ndarray] | None:
     """Node-local gather: rank 0 sizes a file for every sample (float32, original
-    order), each rank writes its own utterances at their offsets, rank 0 reads
-    the whole file back once and removes it."""
+    order), each rank writes its own utterances at their offsets with pwrite,
+    and rank 0 maps the file copy-on-write and removes its name (the mapping
+    outlives it), so the returned arrays are views with no copy back."""
     import torch.distributed as dist
     offsets = np.zeros(len(lengths) + 1, np.int64)
     np.cumsum(np.asarray(lengths, np.int64), out=offsets[1:])
@@ -161,15 +162,22 @@ def _gather_shared_file(local, lengths: list[int], rank: int, group) -> list[np.
     path = name[0]
     try:
         if local and total:
-            mm = np.memmap(path, dtype=np.float32, mode="r+", shape=(total,))
-            for i, pcm in local:
-                mm[offsets[i]:offsets[i + 1]] = np.asarray(pcm, np.float32).reshape(-1)
-            mm.flush()
-            del mm
+            fd = os.open(path, os.O_WRONLY)
+            try:
+                for i, pcm in local:
+                    view = memoryview(np.ascontiguousarray(pcm, dtype=np.float32).reshape(-1)).cast("B")
+                    off = int(offsets[i]) * 4
+                    while len(view):
+                        n = os.pwrite(fd, view, off)
+                        view, off = view[n:], off + n
+            finally:
+                os.close(fd)
         dist.barrier(group=group)
         if rank != 0:
             return None
-        flat = np.fromfile(path, dtype=np.float32, count=total) if total else np.zeros(0, np.float32)
+        if total == 0:
+            return [np.zeros(0, np.float32) for _ in lengths]
+        flat = np.memmap(path, dtype=np.float32, mode="c", shape=(total,))
         return [flat[offsets[i]:offsets[i + 1]] for i in range(len(lengths))]
     finally:
         if rank == 0:

@@ -27,13 +27,21 @@ _i32p = ctypes.POINTER(ctypes.c_int32)
 
 
 def _fp(a):
-    assert a.dtype == np.float32 and a.flags.c_contiguous
+    if a.dtype != np.float32 or not a.flags.c_contiguous:
+        raise TypeError("expected a C-contiguous float32 array")
     return a.ctypes.data_as(_f32p)
 
 
 def _ip(a):
-    assert a.dtype == np.int32 and a.flags.c_contiguous
+    if a.dtype != np.int32 or not a.flags.c_contiguous:
+        raise TypeError("expected a C-contiguous int32 array")
     return a.ctypes.data_as(_i32p)
+
+
+def _check_size(a, n: int, what: str) -> None:
+    # the C ABI reads exactly n elements through the pointer
+    if a.size != n:
+        raise ValueError(f"{what}: expected {n} elements, got shape {a.shape}")
 
 
 class Context:
@@ -86,12 +94,15 @@ class Context:
 
     def decode_features(self, asr, f0, n, style128) -> np.ndarray:
         asr = np.ascontiguousarray(asr, np.float32)
+        if asr.ndim != 2 or asr.shape[1] != 512 or asr.shape[0] < 1:
+            raise ValueError(f"decode_features: asr must be [L, 512] with L >= 1, got shape {asr.shape}")
         L = asr.shape[0]
         f0 = np.ascontiguousarray(f0, np.float32)
         n = np.ascontiguousarray(n, np.float32)
         s = np.ascontiguousarray(style128, np.float32)
-        if f0.shape[0] != 2 * L or n.shape[0] != 2 * L or s.shape[0] != 128:
-            raise ValueError("decode_features: f0/n must be [2L], style [128]")
+        _check_size(f0, 2 * L, "decode_features: f0")
+        _check_size(n, 2 * L, "decode_features: n")
+        _check_size(s, 128, "decode_features: style")
         pcm = np.empty(600 * L, np.float32)
         lib.check(self._L.rk_decode_features(self.h, _fp(asr), _fp(f0), _fp(n), _fp(s), L, _fp(pcm)),
                   "rk_decode_features")
@@ -103,9 +114,14 @@ class Context:
 
     def infer(self, tokens, style256, dur_override=None):
         tok = np.ascontiguousarray(tokens, np.int32)
+        if tok.ndim != 1:
+            raise ValueError(f"infer: tokens must be 1-D, got shape {tok.shape}")
         T = tok.shape[0]
         s = np.ascontiguousarray(style256, np.float32)
+        _check_size(s, 256, "infer: style")
         dov = None if dur_override is None else np.ascontiguousarray(dur_override, np.int32)
+        if dov is not None:
+            _check_size(dov, T, "infer: dur_override")
         dur = np.empty(T, np.int32)
         L = ctypes.c_int(0)
         cap = 600 * (int(dov.sum()) if dov is not None else 64 * T)
@@ -119,12 +135,19 @@ class Context:
         """rk_encode over a batch: utterances have .tokens, .style (256) and
         .durations (used as overrides when `overrides`).  Returns (predicted
         durations per utterance, L per utterance)."""
-        toks = [np.ascontiguousarray(u.tokens, np.int32) for u in utterances]
+        toks = [np.ascontiguousarray(u.tokens, np.int32).reshape(-1) for u in utterances]
         Ts = np.array([t.shape[0] for t in toks], np.int32)
         tok = np.ascontiguousarray(np.concatenate(toks), np.int32)
-        sty = np.ascontiguousarray(np.stack([np.asarray(u.style, np.float32) for u in utterances]), np.float32)
-        dov = (np.ascontiguousarray(np.concatenate([np.asarray(u.durations, np.int32) for u in utterances]), np.int32)
-               if overrides else None)
+        styles = [np.asarray(u.style, np.float32).reshape(-1) for u in utterances]
+        for st in styles:
+            _check_size(st, 256, "encode: style")
+        sty = np.ascontiguousarray(np.stack(styles), np.float32)
+        dov = None
+        if overrides:
+            durs = [np.asarray(u.durations, np.int32).reshape(-1) for u in utterances]
+            for d, t in zip(durs, Ts):
+                _check_size(d, int(t), "encode: durations")
+            dov = np.ascontiguousarray(np.concatenate(durs), np.int32)
         dur = np.empty(tok.shape[0], np.int32)
         Ls = np.empty(len(toks), np.int32)
         lib.check(self._L.rk_encode(self.h, _ip(tok), _ip(Ts), len(toks), _fp(sty),

@@ -73,12 +73,14 @@ def lib():
 
 
 def _fp(a: np.ndarray):
-    assert a.dtype == np.float32 and a.flags.c_contiguous
+    if a.dtype != np.float32 or not a.flags.c_contiguous:
+        raise TypeError("expected a C-contiguous float32 array")
     return a.ctypes.data_as(_f32p)
 
 
 def _ip(a: np.ndarray):
-    assert a.dtype == np.int32 and a.flags.c_contiguous
+    if a.dtype != np.int32 or not a.flags.c_contiguous:
+        raise TypeError("expected a C-contiguous int32 array")
     return a.ctypes.data_as(_i32p)
 
 

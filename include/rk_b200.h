@@ -7,7 +7,12 @@
  * Reference interfaces each entry point replaces (paths in LokalOptima/rokoko):
  *   rk_conv1d_fprop        cutlass_conv1d_fprop / _f16   src/cutlass_conv.cu:239-313,
  *                          src/cutlass_conv_f16.cu:216-273 (same argument meaning
- *                          and return codes 0 / -1 / -2 / -3 / -4)
+ *                          and return codes 0 / -1 / -2 / -3 / -4, plus a precision)
+ *   rk_conv1d_fprop_f32    cutlass_conv1d_fprop      src/cutlass_conv.cu:238-244
+ *   rk_conv1d_fprop_f16    cutlass_conv1d_fprop_f16  src/cutlass_conv_f16.cu:215-221
+ *                          (both with the reference's exact argument list, so a
+ *                          caller of the CUTLASS seam relinks unchanged)
+ *   rk_conv1d_workspace_bytes  cutlass_conv1d_workspace_bytes  src/cutlass_conv.cu:319-330
  *   rk_create + rk_load_weights_koko
  *                          Weights::load + precompute_weight_norms
  *                          src/weights.cpp:500-601, src/rokoko.cpp:1305-1676,
@@ -79,11 +84,31 @@ RK_API rk_status rk_conv1d_fprop(const float* x, const float* w, const float* bi
  * the start of a conv workspace: RK_OK or RK_ERR_DEVICE_TIMEOUT. */
 RK_API rk_status rk_conv1d_check(void* workspace, void* stream);
 
+/* The reference's conv seam, argument for argument (cudaStream_t is passed as
+ * void*; `x` and `w` of the _f16 form point at IEEE half data, the reference's
+ * `const __half*`).  _f32: FP32 operands with FP32 semantics (three split-bf16
+ * tensor-core products per product); _f16: half operands, fp16 products with
+ * FP32 accumulation.  bias, residual and y are FP32 in both, as in the
+ * reference.  The workspace (the reference passes its float* arena slice) must
+ * hold rk_conv1d_workspace_bytes(...) bytes and be 256-byte aligned; its
+ * first 4 bytes are the device error word read by rk_conv1d_check. */
+RK_API rk_status rk_conv1d_fprop_f32(const float* x, const float* w, const float* bias, float* y,
+                                     const float* residual, float* workspace, size_t workspace_bytes, int C_in,
+                                     int C_out, int T_in, int K, int stride, int padding, int dilation,
+                                     void* stream);
+RK_API rk_status rk_conv1d_fprop_f16(const void* x, const void* w, const float* bias, float* y,
+                                     const float* residual, float* workspace, size_t workspace_bytes, int C_in,
+                                     int C_out, int T_in, int K, int stride, int padding, int dilation,
+                                     void* stream);
+/* Workspace bytes for either form above (the larger, FP32, requirement). */
+RK_API size_t rk_conv1d_workspace_bytes(int C_in, int C_out, int T_in, int K, int stride, int padding,
+                                        int dilation);
+
 /* rk_conv1d_fprop without a workspace argument and without any device
  * allocation.  No counterpart in the reference: it exists for callers that
- * cannot allocate device memory where they need the convolution (inside a
- * stream capture, under a host-owned memory pool, on a thread that must not
- * block on the allocator, or within a fixed plugin budget).  Its scratch is one
+ * cannot allocate device memory where they need the convolution (under a
+ * host-owned memory pool, on a thread that must not block on the allocator, or
+ * within a fixed plugin budget).  Its scratch is one
  * library-owned device array of RK_CONV_STATIC_SCRATCH_BYTES on each GPU that
  * loads the library, kept until the process exits; shapes whose
  * rk_conv1d_workspace_size exceeds it return RK_ERR_WORKSPACE.  The first call
@@ -95,6 +120,12 @@ RK_API rk_status rk_conv1d_check(void* workspace, void* stream);
 RK_API rk_status rk_conv1d_fprop_static(const float* x, const float* w, const float* bias, float* y,
                                         const float* residual, int C_in, int C_out, int T_in, int K, int stride,
                                         int padding, int dilation, int precision, void* stream);
+/* Synchronises `stream` and reports (and clears) the device error word of the
+ * static scratch array: RK_ERR_DEVICE_TIMEOUT when a bounded device-side wait
+ * of an rk_conv1d_fprop_static call on this device gave up (its output is then
+ * incomplete), else RK_OK.  Call it after the static calls whose result matters;
+ * each rk_conv1d_fprop_static call clears the word when it starts. */
+RK_API rk_status rk_conv1d_static_check(void* stream);
 
 /* ---- model context ------------------------------------------------------- */
 RK_API rk_status rk_create(int device, const rk_options* opts, rk_ctx** out);

@@ -900,15 +900,19 @@ static InferOut infer(Model& m, const int* tok, int T, const float* style, const
     out.L_b = Lb;
     // alignment as an index gather (build_alignment + NT GEMMs, src/kernels.cu:1484-1505,
     // src/rokoko.cpp:850-863, 916-919): frame l < L copies token row t(l); l >= L is zero.
-    Vec en((size_t)Lb * 640, 0.f), asr((size_t)Lb * 512, 0.f);
+    // frame_token[l] = t(l) for l < L, -1 for the bucket's padding frames (the
+    // column index of the 1 in row t of the reference's 0/1 matrix, src/kernels.cu:1484-1505)
+    Vec en((size_t)Lb * 640, 0.f), asr((size_t)Lb * 512, 0.f), frame_token((size_t)Lb, -1.f);
     {
         int l = 0;
         for (int t = 0; t < T; t++)
             for (int r = 0; r < use[t]; r++, l++) {
                 std::memcpy(&en[(size_t)l * 640], &cat[(size_t)t * 640], 640 * 4);
                 std::memcpy(&asr[(size_t)l * 512], &te[(size_t)t * 512], 512 * 4);
+                frame_token[l] = (float)t;
             }
     }
+    m.dump("frame_token", frame_token);
     Vec sh = bilstm(m, en, Lb, 640, "predictor.shared");
     m.dump("shared", sh);
     auto chain = [&](const char* nm) {

@@ -28,7 +28,6 @@ import datetime
 import json
 import os
 import sys
-import threading
 import time
 
 import numpy as np
@@ -43,6 +42,44 @@ def _args(argv=None):
     p.add_argument("--contexts", type=int, default=2,
                    help="rk_ctx per GPU, each driven by its own host thread on alternating batches")
     return p.parse_args(argv)
+
+
+def run_share(ctxs, utts, indices, batch: int, timings=None):
+    """This rank's share `indices` of `utts` through rk_encode + rk_decode in
+    batches of `batch` (in the given order), dealt round-robin to the contexts
+    `ctxs` (all on this rank's GPU), each context driven by its own host
+    thread.  Returns [(index, PCM)] (context by context); `timings`, if given,
+    receives [encode_s, decode_s] per context."""
+    import threading
+    batches = [indices[k:k + batch] for k in range(0, len(indices), batch)]
+    per_ctx = [batches[c::len(ctxs)] for c in range(len(ctxs))]
+    results = [[] for _ in ctxs]
+    tim = [[0.0, 0.0] for _ in ctxs]
+    errors = []
+
+    def worker(c: int) -> None:
+        try:
+            for idx in per_ctx[c]:
+                te = time.perf_counter()
+                _, Ls = ctxs[c].encode([utts[i] for i in idx])
+                td = time.perf_counter()
+                pcms = ctxs[c].decode(Ls)
+                tim[c][0] += td - te
+                tim[c][1] += time.perf_counter() - td
+                results[c].extend(zip(idx, pcms))
+        except BaseException as e:  # re-raised after the join
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(c,)) for c in range(len(ctxs))]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    if errors:
+        raise errors[0]
+    if timings is not None:
+        timings[:] = tim
+    return [x for r in results for x in r]
 
 
 def main(argv=None) -> int:
@@ -96,32 +133,9 @@ def main(argv=None) -> int:
 
     # one host thread per context: while one context runs the latency-bound front
     # half (encode) of a batch, another's decoders fill the SMs
-    results = [[] for _ in ctxs]
-    timings = [[0.0, 0.0] for _ in ctxs]
-    errors = []
-
-    def worker(c: int) -> None:
-        try:
-            for idx in per_ctx[c]:
-                te = time.perf_counter()
-                _, Ls = ctxs[c].encode([utts[i] for i in idx])
-                td = time.perf_counter()
-                pcms = ctxs[c].decode(Ls)
-                timings[c][0] += td - te
-                timings[c][1] += time.perf_counter() - td
-                results[c].extend(zip(idx, pcms))
-        except BaseException as e:  # re-raised after the join
-            errors.append(e)
-
+    timings = []
     t0 = time.perf_counter()
-    threads = [threading.Thread(target=worker, args=(c,)) for c in range(len(ctxs))]
-    for th in threads:
-        th.start()
-    for th in threads:
-        th.join()
-    if errors:
-        raise errors[0]
-    local_pcm = [x for r in results for x in r]
+    local_pcm = run_share(ctxs, utts, mine, a.batch, timings)
     t_enc = sum(t[0] for t in timings)
     t_dec = sum(t[1] for t in timings)
     t_rank = time.perf_counter() - t0

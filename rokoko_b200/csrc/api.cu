@@ -93,7 +93,6 @@ extern "C" void rk_destroy(rk_ctx* c) {
     DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->side) cudaStreamSynchronize(c->side);
-    for (auto& p : c->pending) cudaFree(p.buf);
     c->pending.clear();
     free_decode_ws(c);
     free_front_ws(c);
@@ -295,55 +294,31 @@ extern "C" size_t rk_compute_decode_bytes(int T, int L) {
 
 namespace {
 
-// Front half + predictor for one utterance (src/rokoko.cpp:829-914): leaves the
-// decoder inputs in ws.asr / ws.f0 / ws.n / ws.style, enqueued on c->stream.
-rk_status encode_one(rk_ctx* c, const int32_t* tokens, int T, const float* style256, const int32_t* dur_override,
-                     int32_t* dur_out, int* L_out, int* Lb_out, const char* who) {
-    std::string w(who);
-    if (!tokens || !style256) return fail(RK_ERR_CANNOT_IMPLEMENT, (w + ": null argument").c_str());
-    if (!c->loaded) return fail(RK_ERR_STATE, (w + ": no weights loaded").c_str());
-    if (!c->has_front)
-        return fail(RK_ERR_WEIGHTS, (w + ": weight file has no front half (ALBERT / predictor)").c_str());
-    if (T < 1 || T > c->max_tokens) return fail(RK_ERR_CANNOT_IMPLEMENT, (w + ": T out of range").c_str());
-    for (int t = 0; t < T; t++)
-        if (tokens[t] < 0 || tokens[t] >= 178)
-            return fail(RK_ERR_CANNOT_IMPLEMENT, (w + ": token id out of range").c_str());
-    if (dur_override)
-        for (int t = 0; t < T; t++)
-            if (dur_override[t] < 0 || dur_override[t] > 4096)
-                return fail(RK_ERR_CANNOT_IMPLEMENT, (w + ": duration override out of range").c_str());
-    rk_status s = ensure_front_tokens(c);
-    if (!s) s = ensure_front_frames(c, std::max(512, c->fws.cap_L));
+// Decoder + generator for one pending utterance: its stashed inputs into the
+// decode workspace, the decode graph for its bucket, PCM (600 L samples) to
+// `pcm` (host, may be null).
+rk_status decode_pending(rk_ctx* c, const rk_ctx::Pending& p, float* pcm, const char* who) {
+    rk_status s = ensure_decode_ws(c, p.L_b);
     if (s) return s;
-    FrontWS& f = c->fws;
+    DecodeWS& w = c->ws;
     cudaStream_t st = c->stream;
-    if (c->record) c->stages.clear();
-    if (cudaMemcpyAsync(f.tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(f.style, style256, 256 * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, (w + ": input upload").c_str());
-    s = enqueue_encode(c, T);
-    if (s) { cudaStreamSynchronize(st); return s; }
-    // predicted durations -> host (the one device -> host dependency of the reference, src/rokoko.cpp:790-793)
-    std::vector<int32_t> pred(T), use(T);
-    if (cudaMemcpyAsync(pred.data(), f.dur_i, (size_t)T * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, (w + ": duration read-back").c_str());
-    long long L = 0;
-    for (int t = 0; t < T; t++) { use[t] = dur_override ? dur_override[t] : pred[t]; L += use[t]; }
-    if (dur_out) std::memcpy(dur_out, pred.data(), (size_t)T * 4);
-    if (L < 1 || L > 64 * 1024) return fail(RK_ERR_CANNOT_IMPLEMENT, (w + ": total duration out of range").c_str());
-    const int bucket = c->l_bucket > 1 ? c->l_bucket : 1;
-    const int L_b = (int)((L + bucket - 1) / bucket * bucket);  // src/rokoko.cpp:797-802
-    *L_out = (int)L;
-    *Lb_out = L_b;
-    s = ensure_decode_ws(c, L_b);
-    if (!s) s = ensure_front_frames(c, L_b);
+    const size_t n_asr = (size_t)p.L_b * 512, n2 = (size_t)2 * p.L_b;
+    if (cudaMemcpyAsync(w.asr, p.asr, n_asr * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.f0, p.f0, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.n, p.n, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(w.style, p.style, 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, (std::string(who) + ": decoder inputs").c_str());
+    s = enqueue_decode(c, p.L_b);
     if (s) return s;
-    if (cudaMemcpyAsync(f.dur_use, use.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, (w + ": duration upload").c_str());
-    s = enqueue_predict(c, T, L_b);
-    if (s) cudaStreamSynchronize(st);
-    return s;
+    const size_t n = (size_t)600 * p.L;
+    if (pcm && cudaMemcpyAsync(pcm, w.audio, n * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, (std::string(who) + ": pcm download").c_str());
+    return RK_OK;
+}
+
+void drop_pending(rk_ctx* c, size_t keep) {
+    c->pending.resize(std::min(keep, c->pending.size()));
+    if (c->pending.empty()) stash_reset(c);
 }
 
 }  // namespace
@@ -353,57 +328,42 @@ extern "C" rk_status rk_infer(rk_ctx* c, const int32_t* tokens, int T, const flo
                               size_t pcm_capacity, size_t* n_samples) {
     if (!c) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_infer: null argument");
     DeviceGuard g(c->device);
-    int L = 0, L_b = 0;
-    rk_status s = encode_one(c, tokens, T, style256, dur_override, dur_out, &L, &L_b, "rk_infer");
-    if (s) return s;
+    const size_t before = c->pending.size();
+    int32_t Tv = T, L = 0;
+    rk_status s = encode_batch(c, tokens, &Tv, 1, style256, dur_override, dur_out, &L, "rk_infer");
+    if (s) { cudaStreamSynchronize(c->stream); drop_pending(c, before); return s; }
     if (L_out) *L_out = L;
-    cudaStream_t st = c->stream;
-    s = enqueue_decode(c, L_b);
-    if (s) { cudaStreamSynchronize(st); return s; }
+    const rk_ctx::Pending p = c->pending.back();
     const size_t n = std::min((size_t)600 * (size_t)L, pcm_capacity);
-    if (pcm && n && cudaMemcpyAsync(pcm, c->ws.audio, n * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, "rk_infer: pcm download");
+    std::vector<float> tmp;
+    float* dst = pcm;
+    if (pcm && n < (size_t)600 * L) { tmp.resize((size_t)600 * L); dst = tmp.data(); }
+    s = decode_pending(c, p, dst, "rk_infer");
+    if (!s) s = check_device_error(c);
+    else cudaStreamSynchronize(c->stream);
+    drop_pending(c, before);
+    if (s) return s;
+    if (pcm && dst != pcm) std::memcpy(pcm, dst, n * 4);
     if (n_samples) *n_samples = pcm ? n : 0;
-    return check_device_error(c);
+    return RK_OK;
 }
 
 // ------------------------------------------------------------------ batched
-// rk_encode runs the front half of B utterances and keeps each one's decoder
-// inputs (aligned features, F0, N, acoustic style) in its own device buffer;
-// rk_decode then runs the decoder for every pending utterance in order.
+// rk_encode runs the front half of B utterances in one pass (encode_batch)
+// and keeps each one's decoder inputs (aligned features, F0, N, acoustic
+// style) in the context's stash; rk_decode then runs the decoder for every
+// pending utterance in order.
 
 extern "C" rk_status rk_encode(rk_ctx* c, const int32_t* tokens, const int32_t* T_per_utt, int B,
                                const float* style, const int32_t* dur_override, int32_t* dur_out, int32_t* L_out) {
     if (!c || !tokens || !T_per_utt || !style || B < 1) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_encode: bad argument");
     DeviceGuard g(c->device);
-    size_t off = 0;
-    for (int b = 0; b < B; b++) {
-        const int T = T_per_utt[b];
-        int L = 0, L_b = 0;
-        rk_status s = encode_one(c, tokens + off, T, style + (size_t)b * 256, dur_override ? dur_override + off : nullptr,
-                                 dur_out ? dur_out + off : nullptr, &L, &L_b, "rk_encode");
-        if (s) return s;
-        if (L_out) L_out[b] = L;
-        // stash the decoder inputs: asr [L_b][512], f0 [2 L_b], n [2 L_b], style [128]
-        const size_t n_asr = (size_t)L_b * 512, n2 = (size_t)2 * L_b;
-        float* buf = nullptr;
-        if (cudaMalloc(&buf, (n_asr + 2 * n2 + 128) * 4) != cudaSuccess) {
-            cudaGetLastError();
-            return fail(RK_ERR_OOM, "rk_encode: pending-utterance buffer");
-        }
-        DecodeWS& w = c->ws;
-        cudaStream_t st = c->stream;
-        if (cudaMemcpyAsync(buf, w.asr, n_asr * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(buf + n_asr, w.f0, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(buf + n_asr + n2, w.n, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(buf + n_asr + 2 * n2, w.style, 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
-            cudaFree(buf);
-            return fail_cuda(RK_ERR_CUDA, "rk_encode: stash");
-        }
-        c->pending.push_back({L, L_b, buf});
-        off += (size_t)T;
-    }
-    return check_device_error(c);
+    const size_t before = c->pending.size();
+    rk_status s = encode_batch(c, tokens, T_per_utt, B, style, dur_override, dur_out, L_out, "rk_encode");
+    if (!s) s = check_device_error(c);
+    else cudaStreamSynchronize(c->stream);
+    if (s) drop_pending(c, before);
+    return s;
 }
 
 extern "C" rk_status rk_decode(rk_ctx* c, float* pcm, size_t pcm_capacity, size_t* n_samples, int* B_out) {
@@ -414,34 +374,17 @@ extern "C" rk_status rk_decode(rk_ctx* c, float* pcm, size_t pcm_capacity, size_
     size_t need = 0;
     for (auto& p : c->pending) need += (size_t)600 * p.L;
     if (pcm && pcm_capacity < need) return fail(RK_ERR_WORKSPACE, "rk_decode: pcm buffer smaller than 600 * sum(L)");
-    cudaStream_t st = c->stream;
     size_t off = 0;
     rk_status s = RK_OK;
     for (int b = 0; b < B && !s; b++) {
         const rk_ctx::Pending& p = c->pending[b];
-        s = ensure_decode_ws(c, p.L_b);
-        if (s) break;
-        DecodeWS& w = c->ws;
-        const size_t n_asr = (size_t)p.L_b * 512, n2 = (size_t)2 * p.L_b;
-        if (cudaMemcpyAsync(w.asr, p.buf, n_asr * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(w.f0, p.buf + n_asr, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(w.n, p.buf + n_asr + n2, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(w.style, p.buf + n_asr + 2 * n2, 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) {
-            s = fail_cuda(RK_ERR_CUDA, "rk_decode: restore");
-            break;
-        }
-        s = enqueue_decode(c, p.L_b);
+        s = decode_pending(c, p, pcm ? pcm + off : nullptr, "rk_decode");
         if (s) break;
         const size_t n = (size_t)600 * p.L;
-        if (pcm && cudaMemcpyAsync(pcm + off, w.audio, n * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
-            s = fail_cuda(RK_ERR_CUDA, "rk_decode: pcm download");
-            break;
-        }
         if (n_samples) n_samples[b] = pcm ? n : 0;
         off += n;
     }
-    cudaStreamSynchronize(st);
-    for (auto& p : c->pending) cudaFree(p.buf);
-    c->pending.clear();
+    cudaStreamSynchronize(c->stream);
+    drop_pending(c, 0);
     return s ? s : check_device_error(c);
 }

@@ -69,7 +69,7 @@ void conv(Run& r, const ConvCall& cc) {
     ops.act_cp = (uint64_t)w.Cp;
     ops.w_hi = w.tm_hi;
     ops.w_lo = w.tm_lo;
-    {   // the split-K scratch of this stream
+    if (!cc.no_splitk) {  // the split-K scratch of this stream
         const cudaStream_t sts[4] = {r.c->stream, r.c->side, r.c->rb[0], r.c->rb[1]};
         for (int i = 0; i < 4; i++)
             if (r.st == sts[i]) { ops.scratch = r.c->splitk[i]; ops.scratch_bytes = rk_ctx::kSplitKBytes; }
@@ -283,6 +283,9 @@ static size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 void free_decode_ws(rk_ctx* c) {
     for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
     c->graphs.clear();
+    // the predictor graphs (F0 / N chains) also bake decode-workspace addresses
+    for (auto& kv : c->pgraphs) cudaGraphExecDestroy(kv.second.exec);
+    c->pgraphs.clear();
     for (void* p : c->ws.allocs) cudaFree(p);
     c->ws = DecodeWS{};
 }

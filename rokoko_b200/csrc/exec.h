@@ -53,6 +53,7 @@ struct ConvCall {
     int o_min = 0;          // first valid output row
     int act = 0;            // 1: GELU after bias
     bool use_bias = true;
+    bool no_splitk = false; // never split the reduction (summation order independent of M)
 };
 
 int stats_parts_for(const ConvCall& cc);

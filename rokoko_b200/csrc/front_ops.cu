@@ -1,13 +1,16 @@
 // front_ops.cu -- bandwidth / latency kernels of the front half (ALBERT, text
-// encoder, prosody predictor) and the duration -> alignment expansion.
+// encoder, prosody predictor) and the duration -> alignment expansion, over
+// every utterance of a batch at once (segmented row layout, front_ops.cuh).
 //
 // Reference semantics (src/kernels.cu): embeddings + LayerNorm :15-95,
 // residual LayerNorm :102-144, softmax :189-225, channel LayerNorm :364-404,
 // AdaLayerNorm :513-548, sigmoid-sum :643-662, round/clamp durations
-// :1457-1479, alignment :1484-1505 (here an index gather instead of a dense 0/1
-// matrix and two GEMMs, src/rokoko.cpp:850-863, 916-919).
+// :1457-1479, alignment :1484-1505 (here a scan + index gather instead of a
+// dense 0/1 matrix and two GEMMs, src/rokoko.cpp:850-863, 916-919).
 // Row kernels use one warp per row with the two-pass mean / variance of the
-// reference, and write the next GEMM's 16-bit operand planes directly.
+// reference, and write the next GEMM's 16-bit operand planes directly.  The
+// arithmetic of a row does not depend on the batch it is in, so an utterance
+// gives the same bits alone or batched.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -46,18 +49,27 @@ __device__ __forceinline__ void row_stats(const float (&v)[VPL], int D, float& m
     inv = rsqrtf(warp_sum(q) / D + eps);
 }
 
-__global__ void embed_ln_kernel(const int* __restrict__ tok, int T, const float* __restrict__ word,
-                                const float* __restrict__ pos, const float* __restrict__ type,
-                                const float* __restrict__ g, const float* __restrict__ b, float* __restrict__ out,
-                                OpPlanes op, bool split) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
+// zeros for a gap row: the FP32 output row (length D, pitch ldo) and the operand columns [0, Cp)
+__device__ __forceinline__ void zero_row(float* out, int ldo, int D, int r, OpPlanes op, bool split, int lane) {
+    for (int d = lane; d < D; d += 32)
+        if (out) out[(size_t)r * ldo + d] = 0.f;
+    for (int d = lane; d < op.Cp; d += 32) put_op(op.hi, op.lo, (size_t)r * op.Cp + d, 0.f, split);
+}
+
+__global__ void embed_ln_kernel(RowMeta m, const float* __restrict__ word, const float* __restrict__ pos,
+                                const float* __restrict__ type, const float* __restrict__ g,
+                                const float* __restrict__ b, float* __restrict__ out, OpPlanes op, bool split) {
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= m.R) return;
     constexpr int D = 128, VPL = 4;
+    const int p = m.pos[r];
+    if (p < 0) { zero_row(out, D, D, r, op, split, lane); return; }
+    const int tk = m.tok[r];
     float v[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; i++) {
         const int d = lane + 32 * i;
-        v[i] = (word[(size_t)tok[t] * D + d] + pos[(size_t)t * D + d]) + type[d];
+        v[i] = (word[(size_t)tk * D + d] + pos[(size_t)p * D + d]) + type[d];
     }
     float mean, inv;
     row_stats<VPL>(v, D, mean, inv, 1e-12f);
@@ -65,21 +77,22 @@ __global__ void embed_ln_kernel(const int* __restrict__ tok, int T, const float*
     for (int i = 0; i < VPL; i++) {
         const int d = lane + 32 * i;
         const float y = (v[i] - mean) * inv * g[d] + b[d];
-        out[(size_t)t * D + d] = y;
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + d, y, split);
+        out[(size_t)r * D + d] = y;
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + d, y, split);
     }
 }
 
 // h = LN(h + a) (eps 1e-12), D = 768; also the next GEMM's operand
-__global__ void res_ln_kernel(float* __restrict__ h, const float* __restrict__ a, int T,
+__global__ void res_ln_kernel(float* __restrict__ h, const float* __restrict__ a, RowMeta m,
                               const float* __restrict__ g, const float* __restrict__ b, OpPlanes op, bool split) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= m.R) return;
     constexpr int D = 768, VPL = 24;
+    if (m.pos[r] < 0) { zero_row(h, D, D, r, op, split, lane); return; }
     float v[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; i++) {
-        const size_t o = (size_t)t * D + lane + 32 * i;
+        const size_t o = (size_t)r * D + lane + 32 * i;
         v[i] = h[o] + a[o];
     }
     float mean, inv;
@@ -88,20 +101,21 @@ __global__ void res_ln_kernel(float* __restrict__ h, const float* __restrict__ a
     for (int i = 0; i < VPL; i++) {
         const int d = lane + 32 * i;
         const float y = (v[i] - mean) * inv * g[d] + b[d];
-        h[(size_t)t * D + d] = y;
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + d, y, split);
+        h[(size_t)r * D + d] = y;
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + d, y, split);
     }
 }
 
 // text encoder: y = LeakyReLU(LN_channels(x) * gamma + beta, 0.2), D = 512
-__global__ void ln_lrelu_kernel(const float* __restrict__ x, int T, const float* __restrict__ g,
+__global__ void ln_lrelu_kernel(const float* __restrict__ x, RowMeta m, const float* __restrict__ g,
                                 const float* __restrict__ b, float* __restrict__ out, OpPlanes op, bool split) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= m.R) return;
     constexpr int D = 512, VPL = 16;
+    if (m.pos[r] < 0) { zero_row(out, D, D, r, op, split, lane); return; }
     float v[VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; i++) v[i] = x[(size_t)t * D + lane + 32 * i];
+    for (int i = 0; i < VPL; i++) v[i] = x[(size_t)r * D + lane + 32 * i];
     float mean, inv;
     row_stats<VPL>(v, D, mean, inv, 1e-5f);
 #pragma unroll
@@ -109,22 +123,26 @@ __global__ void ln_lrelu_kernel(const float* __restrict__ x, int T, const float*
         const int d = lane + 32 * i;
         float y = (v[i] - mean) * inv * g[d] + b[d];
         y = y > 0.f ? y : 0.2f * y;
-        out[(size_t)t * D + d] = y;
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + d, y, split);
+        out[(size_t)r * D + d] = y;
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + d, y, split);
     }
 }
 
-// cat[t] = [x[t] (AdaLN'd when gamma != null) | style]  (D = 512 + 128)
-__global__ void adaln_concat_kernel(const float* __restrict__ x, int T, const float* __restrict__ gamma,
-                                    const float* __restrict__ beta, const float* __restrict__ style,
+// cat[r] = [x[r] (AdaLN'd when gamma_off >= 0) | style]  (D = 512 + 128)
+__global__ void adaln_concat_kernel(const float* __restrict__ x, RowMeta m, const float* __restrict__ fc,
+                                    int fc_stride, int gamma_off, const float* __restrict__ style, int style_stride,
                                     float* __restrict__ cat, OpPlanes op, bool split) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= m.R) return;
     constexpr int D = 512, VPL = 16;
+    const int u = m.utt[r];
+    if (u < 0) { zero_row(cat, 640, 640, r, op, split, lane); return; }
     float v[VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; i++) v[i] = x[(size_t)t * D + lane + 32 * i];
-    if (gamma) {
+    for (int i = 0; i < VPL; i++) v[i] = x[(size_t)r * D + lane + 32 * i];
+    if (gamma_off >= 0) {
+        const float* gamma = fc + (size_t)u * fc_stride + gamma_off;
+        const float* beta = gamma + 512;
         float mean, inv;
         row_stats<VPL>(v, D, mean, inv, 1e-5f);
 #pragma unroll
@@ -136,25 +154,31 @@ __global__ void adaln_concat_kernel(const float* __restrict__ x, int T, const fl
 #pragma unroll
     for (int i = 0; i < VPL; i++) {
         const int d = lane + 32 * i;
-        cat[(size_t)t * 640 + d] = v[i];
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + d, v[i], split);
+        cat[(size_t)r * 640 + d] = v[i];
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + d, v[i], split);
     }
+    const float* s = style + (size_t)u * style_stride;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int d = lane + 32 * i;
-        cat[(size_t)t * 640 + 512 + d] = style[d];
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + 512 + d, style[d], split);
+        cat[(size_t)r * 640 + 512 + d] = s[d];
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + 512 + d, s[d], split);
     }
 }
 
 // Scaled dot-product attention without mask, FP32 (src/rokoko.cpp:363-384):
-// S = Q K^T * 0.125, softmax over keys, O = P V.  Block = 8 warps = 8 query
-// rows of one head; keys / values staged through shared memory in chunks.
+// S = Q K^T * 0.125, softmax over keys, O = P V, within utterance blockIdx.z.
+// Block = 8 warps = 8 query rows of one head; keys / values staged through
+// shared memory in chunks.
 constexpr int ATT_ROWS = 8, ATT_CHUNK = 64, ATT_MAXT = 512;
-__global__ void attention_kernel(const float* __restrict__ qkv, int T, float* __restrict__ ctx) {
+__global__ void attention_kernel(const float* __restrict__ qkv_all, SegMeta s, float* __restrict__ ctx_all) {
     __shared__ float kv[ATT_CHUNK][65];
     __shared__ float sc[ATT_ROWS][ATT_MAXT];
     __shared__ float qs[ATT_ROWS][64];
+    const int T = s.len[blockIdx.z];
+    if ((int)blockIdx.x * ATT_ROWS >= T) return;  // uniform over the block
+    const float* qkv = qkv_all + (size_t)s.off[blockIdx.z] * 2304;
+    float* ctx = ctx_all + (size_t)s.off[blockIdx.z] * 768;
     const int head = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * ATT_ROWS + w;
     const bool row_ok = i < T;
@@ -186,13 +210,13 @@ __global__ void attention_kernel(const float* __restrict__ qkv, int T, float* __
         for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sc[w][j]);
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float s = 0.f;
+        float sum = 0.f;
         for (int j = lane; j < T; j += 32) {
             const float e = expf(sc[w][j] - mx);
             sc[w][j] = e;
-            s += e;
+            sum += e;
         }
-        inv = 1.0f / warp_sum(s);
+        inv = 1.0f / warp_sum(sum);
     }
     // O = P V
     float o0 = 0.f, o1 = 0.f;
@@ -217,49 +241,74 @@ __global__ void attention_kernel(const float* __restrict__ qkv, int T, float* __
     }
 }
 
-// dur[t] = sum_50 sigmoid(proj[t]); int = max(1, round-half-even(dur))
-__global__ void durations_kernel(const float* __restrict__ proj, int T, float* __restrict__ dur_f,
+// dur[r] = sum_50 sigmoid(proj[r]); int = max(1, round-half-even(dur)); gap rows 0
+__global__ void durations_kernel(const float* __restrict__ proj, RowMeta m, float* __restrict__ dur_f,
                                  int* __restrict__ dur_i) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= T) return;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= m.R) return;
+    if (m.pos[r] < 0) {
+        if (lane == 0) { dur_f[r] = 0.f; dur_i[r] = 0; }
+        return;
+    }
     float s = 0.f;
-    for (int d = lane; d < 50; d += 32) s += 1.0f / (1.0f + expf(-proj[(size_t)t * 50 + d]));
+    for (int d = lane; d < 50; d += 32) s += 1.0f / (1.0f + expf(-proj[(size_t)r * 50 + d]));
     s = warp_sum(s);
     if (lane == 0) {
-        dur_f[t] = s;
-        dur_i[t] = max(1, __float2int_rn(s));
+        dur_f[r] = s;
+        dur_i[r] = max(1, __float2int_rn(s));
     }
 }
 
-// Alignment as an index gather: frame l of token t(l) where token t covers
-// frames [sum_{i<t} d_i, sum_{i<=t} d_i).  en[l] = cat[t(l)] (640, also as the
-// shared LSTM's operand), asr[l] = te[t(l)] (512); frames >= L are zero.
-__global__ void align_gather_kernel(const int* __restrict__ dur, int T, int L_b, const float* __restrict__ cat,
-                                    const float* __restrict__ te, float* __restrict__ en, float* __restrict__ asr,
-                                    OpPlanes op, bool split) {
+// One block per (frame chunk, utterance): the block scans the utterance's
+// durations (exclusive prefix sums in shared memory, integer so exact), then
+// its frames find their token by binary search.
+constexpr int ALIGN_THREADS = 256;
+__global__ void __launch_bounds__(ALIGN_THREADS) align_gather_kernel(
+    const int* __restrict__ dur, SegMeta tok, SegMeta frames, const float* __restrict__ cat,
+    const float* __restrict__ te, float* __restrict__ en, float* __restrict__ asr, int* __restrict__ frame_tok,
+    OpPlanes op, bool split) {
     __shared__ int start[ATT_MAXT + 1];
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int t = 0; t < T; t++) { start[t] = acc; acc += dur[t]; }
-        start[T] = acc;
+    __shared__ int warp_tot[ALIGN_THREADS / 32];
+    const int u = blockIdx.y;
+    const int T = tok.len[u], toff = tok.off[u];
+    const int Lb = frames.len[u], foff = frames.off[u];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // thread i holds durations 2i and 2i + 1 (T <= 512 = 2 x 256)
+    const int a = 2 * tid < T ? dur[toff + 2 * tid] : 0;
+    const int b = 2 * tid + 1 < T ? dur[toff + 2 * tid + 1] : 0;
+    int incl = a + b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
     }
+    if (lane == 31) warp_tot[wid] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int k = 0; k < wid; k++) before += warp_tot[k];
+    const int excl = before + incl - (a + b);
+    if (2 * tid < T) start[2 * tid] = excl;
+    if (2 * tid + 1 < T) start[2 * tid + 1] = excl + a;
+    if (tid == ALIGN_THREADS - 1) start[T] = before + incl;  // total L (zeros past T add nothing)
     __syncthreads();
     const int L = start[T];
-    for (int l = blockIdx.x; l < L_b; l += gridDim.x) {
-        int tok = -1;
-        if (l < L) {  // binary search: largest t with start[t] <= l
+    for (int l = blockIdx.x; l < Lb; l += gridDim.x) {
+        int t = -1;
+        if (l < L) {  // largest t with start[t] <= l
             int lo = 0, hi = T - 1;
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
                 if (start[mid] <= l) lo = mid; else hi = mid - 1;
             }
-            tok = lo;
+            t = lo;
         }
-        for (int d = threadIdx.x; d < 640; d += blockDim.x) {
-            const float v = tok >= 0 ? cat[(size_t)tok * 640 + d] : 0.f;
-            en[(size_t)l * 640 + d] = v;
-            put_op(op.hi, op.lo, (size_t)l * op.Cp + d, v, split);
-            if (d < 512) asr[(size_t)l * 512 + d] = tok >= 0 ? te[(size_t)tok * 512 + d] : 0.f;
+        const size_t f = (size_t)foff + l;
+        if (tid == 0) frame_tok[f] = t;
+        for (int d = tid; d < 640; d += ALIGN_THREADS) {
+            const float v = t >= 0 ? cat[(size_t)(toff + t) * 640 + d] : 0.f;
+            en[f * 640 + d] = v;
+            put_op(op.hi, op.lo, f * op.Cp + d, v, split);
+            if (d < 512) asr[f * 512 + d] = t >= 0 ? te[(size_t)(toff + t) * 512 + d] : 0.f;
         }
     }
 }
@@ -275,53 +324,60 @@ __global__ void rowdot_kernel(const float* __restrict__ x, int T, int C, const f
     if (lane == 0) y[t] = s + b[0];
 }
 
-__global__ void gather_rows_kernel(const int* __restrict__ tok, int T, const float* __restrict__ table, int D,
-                                   float* __restrict__ out, OpPlanes op, bool split) {
-    const int t = blockIdx.x;
-    if (t >= T) return;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        const float v = table[(size_t)tok[t] * D + d];
-        out[(size_t)t * D + d] = v;
-        put_op(op.hi, op.lo, (size_t)t * op.Cp + d, v, split);
+__global__ void gather_rows_kernel(RowMeta m, const float* __restrict__ table, int D, float* __restrict__ out,
+                                   OpPlanes op, bool split) {
+    const int r = blockIdx.x;
+    if (r >= m.R) return;
+    const bool gap = m.pos[r] < 0;
+    const int tk = m.tok[r];
+    for (int d = threadIdx.x; d < op.Cp; d += blockDim.x) {
+        const float v = (!gap && d < D) ? table[(size_t)tk * D + d] : 0.f;
+        if (d < D) out[(size_t)r * D + d] = v;
+        put_op(op.hi, op.lo, (size_t)r * op.Cp + d, v, split);
     }
 }
 
-int rows_grid(int T) { return (T + 7) / 8; }
+int rows_grid(int R) { return (R + 7) / 8; }
 
 }  // namespace
 
-void embed_ln(const int* tok, int T, const float* word, const float* pos, const float* type, const float* g,
-              const float* b, float* out, OpPlanes op, bool split, cudaStream_t st) {
-    embed_ln_kernel<<<rows_grid(T), 256, 0, st>>>(tok, T, word, pos, type, g, b, out, op, split);
+void embed_ln(RowMeta m, const float* word, const float* pos, const float* type, const float* g, const float* b,
+              float* out, OpPlanes op, bool split, cudaStream_t st) {
+    embed_ln_kernel<<<rows_grid(m.R), 256, 0, st>>>(m, word, pos, type, g, b, out, op, split);
 }
-void res_ln(float* h, const float* a, int T, const float* g, const float* b, OpPlanes op, bool split,
+void res_ln(float* h, const float* a, RowMeta m, const float* g, const float* b, OpPlanes op, bool split,
             cudaStream_t st) {
-    res_ln_kernel<<<rows_grid(T), 256, 0, st>>>(h, a, T, g, b, op, split);
+    res_ln_kernel<<<rows_grid(m.R), 256, 0, st>>>(h, a, m, g, b, op, split);
 }
-void ln_lrelu(const float* x, int T, const float* g, const float* b, float* out, OpPlanes op, bool split,
+void ln_lrelu(const float* x, RowMeta m, const float* g, const float* b, float* out, OpPlanes op, bool split,
               cudaStream_t st) {
-    ln_lrelu_kernel<<<rows_grid(T), 256, 0, st>>>(x, T, g, b, out, op, split);
+    ln_lrelu_kernel<<<rows_grid(m.R), 256, 0, st>>>(x, m, g, b, out, op, split);
 }
-void adaln_concat(const float* x, int T, const float* gamma, const float* beta, const float* style, float* cat,
-                  OpPlanes op, bool split, cudaStream_t st) {
-    adaln_concat_kernel<<<rows_grid(T), 256, 0, st>>>(x, T, gamma, beta, style, cat, op, split);
+void adaln_concat(const float* x, RowMeta m, const float* fc, int fc_stride, int gamma_off, const float* style,
+                  int style_stride, float* cat, OpPlanes op, bool split, cudaStream_t st) {
+    adaln_concat_kernel<<<rows_grid(m.R), 256, 0, st>>>(x, m, fc, fc_stride, gamma_off, style, style_stride, cat, op,
+                                                         split);
 }
-void attention(const float* qkv, int T, float* ctx, cudaStream_t st) {
-    attention_kernel<<<dim3((T + ATT_ROWS - 1) / ATT_ROWS, 12), 32 * ATT_ROWS, 0, st>>>(qkv, T, ctx);
+void attention(const float* qkv, SegMeta s, float* ctx, cudaStream_t st) {
+    attention_kernel<<<dim3((s.max_len + ATT_ROWS - 1) / ATT_ROWS, 12, s.n), 32 * ATT_ROWS, 0, st>>>(qkv, s, ctx);
 }
-void durations(const float* proj, int T, float* dur_f, int* dur_i, cudaStream_t st) {
-    durations_kernel<<<rows_grid(T), 256, 0, st>>>(proj, T, dur_f, dur_i);
+void durations(const float* proj, RowMeta m, float* dur_f, int* dur_i, cudaStream_t st) {
+    durations_kernel<<<rows_grid(m.R), 256, 0, st>>>(proj, m, dur_f, dur_i);
 }
-void align_gather(const int* dur, int T, int L_b, const float* cat, const float* te, float* en, float* asr,
-                  OpPlanes op, bool split, cudaStream_t st) {
-    align_gather_kernel<<<148 * 2, 256, 0, st>>>(dur, T, L_b, cat, te, en, asr, op, split);
+void align_gather(const int* dur, SegMeta tok, SegMeta frames, const float* cat, const float* te, float* en,
+                  float* asr, int* frame_tok, OpPlanes op, bool split, cudaStream_t st) {
+    // frame chunks per utterance: about two waves of blocks over the whole batch
+    int chunks = (148 * 4 + frames.n - 1) / frames.n;
+    if (chunks > frames.max_len) chunks = frames.max_len;
+    if (chunks < 1) chunks = 1;
+    align_gather_kernel<<<dim3(chunks, frames.n), ALIGN_THREADS, 0, st>>>(dur, tok, frames, cat, te, en, asr,
+                                                                         frame_tok, op, split);
 }
 void rowdot(const float* x, int T, int C, const float* w, const float* b, float* y, cudaStream_t st) {
     rowdot_kernel<<<rows_grid(T), 256, 0, st>>>(x, T, C, w, b, y);
 }
-void gather_rows(const int* tok, int T, const float* table, int D, float* out, OpPlanes op, bool split,
-                 cudaStream_t st) {
-    gather_rows_kernel<<<T, 256, 0, st>>>(tok, T, table, D, out, op, split);
+void gather_rows(RowMeta m, const float* table, int D, float* out, OpPlanes op, bool split, cudaStream_t st) {
+    gather_rows_kernel<<<m.R, 256, 0, st>>>(m, table, D, out, op, split);
 }
 
 }  // namespace rk

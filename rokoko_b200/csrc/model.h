@@ -140,18 +140,35 @@ struct DecodeWS {
     Operand op_har0, op_har1;
 };
 
-// Front-half workspace: token-sized buffers (allocs) and frame-sized buffers
-// (frame_allocs, grown with the decode length).
+// Front-half workspace.  Three groups, each grown on demand:
+//   rows    token rows of a batch in the segmented layout (front_ops.cuh):
+//           cap_R rows, cap_B utterances;
+//   frames  decoder frames of a batch (utterance b's L_b frames at frame_off[b]):
+//           cap_F rows, plus the LSTM input-gate and operand buffers sized for
+//           both row and frame phases;
+//   pred    one utterance's predictor (F0 / N chains) of up to cap_Lb frames;
+//           the predictor graphs bake these addresses.
 struct FrontWS {
-    std::vector<void*> allocs, frame_allocs;
-    int cap_L = 0;
-    int *tok = nullptr, *dur_i = nullptr, *dur_use = nullptr;
-    float *style = nullptr, *dur_f = nullptr, *emb = nullptr, *h = nullptr, *qkv = nullptr, *ctx = nullptr,
-          *tmp = nullptr, *ffmid = nullptr, *d_en = nullptr, *te = nullptr, *tbuf = nullptr, *cat = nullptr,
-          *lstm_out = nullptr, *proj = nullptr;
-    float *ig = nullptr, *en = nullptr, *shared = nullptr, *x1 = nullptr, *x2 = nullptr, *x3 = nullptr,
-          *stats = nullptr, *stats2 = nullptr;
+    int cap_R = 0, cap_B = 0;
+    std::vector<void*> row_allocs;
+    int* meta = nullptr;  // tok[R] | pos[R] | utt[R] | seg_off[B] | seg_len[B] | dur_use[R] | f_off[B] | f_len[B]
+    int* dur_i = nullptr;
+    float *style = nullptr, *fc = nullptr, *dur_f = nullptr, *emb = nullptr, *h = nullptr, *qkv = nullptr,
+          *ctx = nullptr, *tmp = nullptr, *ffmid = nullptr, *d_en = nullptr, *te = nullptr, *tbuf = nullptr,
+          *cat = nullptr, *lstm_out = nullptr, *proj = nullptr;
+    int cap_F = 0;
+    std::vector<void*> frame_allocs;
+    float *en = nullptr, *shared_all = nullptr;
+    int* frame_tok = nullptr;
+    size_t cap_ig = 0, cap_op = 0;  // rows of ig; bytes of one operand plane
+    std::vector<void*> ig_allocs;
+    float* ig = nullptr;            // [rows][2048] LSTM input gates
     Operand op;
+    int len0 = 0;                   // token count of the batch's first utterance (stage capture)
+    int cap_Lb = 0;
+    std::vector<void*> pred_allocs;
+    float *shared = nullptr, *x1 = nullptr, *x2 = nullptr, *x3 = nullptr, *stats = nullptr, *stats2 = nullptr,
+          *style1 = nullptr, *f0 = nullptr, *n = nullptr;
 };
 
 struct StageRec {  // captured stage activations (rk_record_stages)
@@ -219,10 +236,21 @@ struct rk_ctx {
     std::vector<double> prof_flops;        // algorithmic FLOPs of each timed launch
     double prof_ms_acc = 0.0, prof_flops_acc = 0.0;
     long long prof_launches_acc = 0;
-    // utterances encoded by rk_encode and not yet decoded: decoder inputs in one device buffer each
+    // predictor graphs (one utterance's F0 / N chains) keyed by L_b
+    std::map<int, GraphRec> pgraphs;
+    // utterances encoded by rk_encode and not yet decoded: their decoder inputs
+    // (asr [L_b][512], f0 / n [2 L_b], style [128]) live in the stash chunks
     struct Pending {
         int L, L_b;
-        float* buf;
+        float *asr, *f0, *n, *style;
     };
     std::vector<Pending> pending;
+    struct StashChunk {
+        char* base;
+        size_t bytes, used;
+    };
+    std::vector<StashChunk> stash;
+    // pinned host staging for the batch metadata upload and the duration read-back
+    void* h_stage = nullptr;
+    size_t h_stage_bytes = 0;
 };

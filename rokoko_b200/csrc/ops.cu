@@ -37,10 +37,14 @@ int nblocks(long work, int threads, int cap = 148 * 16) {
 // element counts for which a 32-bit grid-stride index cannot overflow
 bool small_index(long total) { return total < (1L << 31) - 148L * 16 * 1024; }
 
+// one warp per (style-FC row, utterance blockIdx.y)
 __global__ void style_fc_kernel(const float* __restrict__ W, const float* __restrict__ b,
-                                const float* __restrict__ s, float* __restrict__ out, int rows) {
+                                const float* __restrict__ s_all, int s_stride, float* __restrict__ out_all,
+                                int rows) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
+    const float* s = s_all + (size_t)blockIdx.y * s_stride;
+    float* out = out_all + (size_t)blockIdx.y * rows;
     const float* w = W + (size_t)warp * 128;
     float acc = 0.f;
 #pragma unroll
@@ -363,7 +367,12 @@ __global__ void istft_ola_kernel(const float* __restrict__ fr, int T2, float* __
 }  // namespace
 
 void style_fc(const float* W, const float* b, const float* s, float* out, int rows, cudaStream_t st) {
-    style_fc_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(W, b, s, out, rows);
+    style_fc_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(W, b, s, 0, out, rows);
+}
+
+void style_fc_batch(const float* W, const float* b, const float* s, int s_stride, int B, float* out, int rows,
+                    cudaStream_t st) {
+    style_fc_kernel<<<dim3((rows * 32 + 255) / 256, B), 256, 0, st>>>(W, b, s, s_stride, out, rows);
 }
 
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,

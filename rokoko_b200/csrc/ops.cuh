@@ -7,6 +7,9 @@ namespace rk {
 
 // out[r] = W[r,:] . s + b[r]  for all style-FC rows of one style half.
 void style_fc(const float* W, const float* b, const float* s, float* out, int rows, cudaStream_t st);
+// The same for B style vectors s + u*s_stride: out[u*rows + r] (bit-identical per utterance).
+void style_fc_batch(const float* W, const float* b, const float* s, int s_stride, int B, float* out, int rows,
+                    cudaStream_t st);
 
 // AdaIN coefficients from per-part column sums: stats[p*ld + c] (sums) and
 // stats[(parts+p)*ld + c] (squares), c in [col0, col0+C).

@@ -43,6 +43,12 @@ SIGNATURES = [
      [ctypes.c_void_p] * 5 + [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
     ("rk_conv1d_check", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ("rk_conv1d_fprop_static", ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
+    ("rk_conv1d_static_check", ctypes.c_int, [ctypes.c_void_p]),
+    ("rk_conv1d_fprop_f32", ctypes.c_int,
+     [ctypes.c_void_p] * 5 + [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 7 + [ctypes.c_void_p]),
+    ("rk_conv1d_fprop_f16", ctypes.c_int,
+     [ctypes.c_void_p] * 5 + [ctypes.c_void_p, ctypes.c_size_t] + [ctypes.c_int] * 7 + [ctypes.c_void_p]),
+    ("rk_conv1d_workspace_bytes", ctypes.c_size_t, [ctypes.c_int] * 7),
     ("rk_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(rk_options), ctypes.POINTER(ctypes.c_void_p)]),
     ("rk_destroy", None, [ctypes.c_void_p]),
     ("rk_load_weights_koko", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]),

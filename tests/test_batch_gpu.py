@@ -1,7 +1,8 @@
 """Batched entry points (rk_encode + rk_decode) on the B200: every utterance
-of a batch comes out bit-identical to its own rk_infer call (the kernels are
-deterministic), and the batch holds utterances of different lengths (so of
-different decoder-frame buckets)."""
+of a batch comes out bit-identical to its own rk_infer call (the front half's
+arithmetic per utterance does not depend on the batch: no split reductions,
+per-sequence LSTM sums in a fixed order), and the batch holds utterances of
+different lengths (so of different decoder-frame buckets)."""
 import numpy as np
 import pytest
 
@@ -66,3 +67,25 @@ def test_two_contexts_on_two_threads_match_one_context(v1_blob):
     finally:
         for c in ctxs:
             c.close()
+
+
+@pytest.mark.parametrize("overrides", [True, False])
+def test_large_batch_fp16_bit_identical_to_single(v1_blob, overrides):
+    """40 utterances of different lengths in one rk_encode (the BiLSTM kernel
+    then packs eight sequences per cluster): every utterance's durations, L and
+    PCM equal its own rk_infer call bit for bit, with the durations given and
+    with the durations the model predicts."""
+    from rokoko_b200 import configs, convert_v2
+    from rokoko_b200.context import FP16, Context
+    batch = [configs.config0(seed=100 + k, n_phon=3 + (k * 7) % 29) for k in range(40)]
+    v2 = convert_v2.convert_blob(v1_blob)
+    with Context(0, FP16) as ctx:
+        ctx.load_weights(v2)
+        durs, Ls = ctx.encode(batch, overrides=overrides)
+        pcms = ctx.decode(Ls)
+        assert len(pcms) == len(batch)
+        for u, d, L, pcm in zip(batch, durs, Ls, pcms):
+            ref, ref_dur, ref_L = ctx.infer(u.tokens, u.style, u.durations if overrides else None)
+            assert L == ref_L
+            assert np.array_equal(d, ref_dur)
+            assert np.array_equal(pcm, ref)

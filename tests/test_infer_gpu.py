@@ -3,8 +3,10 @@
 Bars: predicted durations bit-exact, L and the sample count (600 L) exact,
 per-stage activations close, waveform relative L2 <= 1e-3 (FP32 semantics).
 Config 0 shapes: 64 phonemes (T = 66), durations overridden by seeded U[2,8]
-(so L ~ 330 -> bucket 352); a smaller T = 20 case runs the predicted
-durations (no override) through the whole pipeline.
+(so L ~ 330 -> bucket 352), and the same T = 66 with the predicted durations
+(no override) through the whole pipeline, as a smaller T = 20 case.  The
+alignment indices (frame -> token, -1 for the bucket's padding frames) are
+compared exactly.
 """
 import numpy as np
 import pytest
@@ -40,7 +42,7 @@ def gpu_ctx(v1_blob):
     ctx.close()
 
 
-@pytest.mark.parametrize("n_phon,override", [(64, True), (18, False)])
+@pytest.mark.parametrize("n_phon,override", [(64, True), (64, False), (18, False)])
 def test_infer_fp32(gpu_ctx, oracle_model, n_phon, override):
     from rokoko_b200 import configs
     u = configs.config0(seed=n_phon, n_phon=n_phon)
@@ -49,7 +51,12 @@ def test_infer_fp32(gpu_ctx, oracle_model, n_phon, override):
     pcm, dur, L = gpu_ctx.infer(u.tokens, u.style, dov)
     assert np.array_equal(dur, ref_dur), (dur, ref_dur)
     assert L == ref_L
+    if override:
+        assert L == int(u.durations.sum())
     assert pcm.shape == ref.shape == (600 * L,)
+    ft, ref_ft = gpu_ctx.stage("frame_token"), oracle_model.stage("frame_token")
+    assert ft is not None and ref_ft is not None
+    assert np.array_equal(ft, ref_ft), "alignment indices differ"
     report = []
     for name, tol in STAGES:
         g, o = gpu_ctx.stage(name), oracle_model.stage(name)

@@ -1,13 +1,14 @@
 """rk_conv1d_fprop_static: the convolution entry point that allocates nothing.
 
 It serves callers that cannot allocate device memory where they need a
-convolution (a stream being captured into a CUDA graph, a host whose device
-memory comes from its own pool, a thread that must not block on the allocator,
-a fixed plugin budget).  Its scratch lives in one library-owned device array, so
-these tests check that (1) two calls in a row through the C ABI give the same
-result as rk_conv1d_fprop with a caller-provided workspace, within the
-tolerance of the other conv tests, and (2) a shape larger than the array is
-rejected with RK_ERR_WORKSPACE without touching the output.
+convolution (a host whose device memory comes from its own pool, a thread that
+must not block on the allocator, a fixed plugin budget).  Its scratch lives in
+one library-owned device array, so these tests check that (1) two calls in a
+row through the C ABI give the same result as rk_conv1d_fprop with a
+caller-provided workspace (the same kernels with the same tiling, so bit for
+bit, which is inside the 2e-5 tolerance of the other conv tests), and that
+rk_conv1d_static_check then reports a clean error word, and (2) a shape larger
+than the array is rejected with RK_ERR_WORKSPACE without touching the output.
 
 This file is named so that pytest collects it last.
 """
@@ -55,10 +56,13 @@ def test_static_scratch_matches_workspace_entry(rk_lib):
                                                 C_in, C_out, T_in, K, 1, pad, dil, prec, st),
                   "rk_conv1d_fprop_static")
         torch.cuda.synchronize()
+        lib.check(rk_lib.rk_conv1d_static_check(st), "rk_conv1d_static_check")
+        lib.check(rk_lib.rk_conv1d_check(wp, st), "rk_conv1d_check")
         a, e = y_st.double().cpu(), y_ws.double().cpu()
         assert torch.isfinite(a).all()
         rel = float((a - e).norm() / e.norm())
         assert rel <= TOL, (seed, rel)
+        assert torch.equal(y_st, y_ws), seed
 
 
 def test_static_scratch_rejects_oversize(rk_lib):

@@ -1,25 +1,48 @@
 #!/usr/bin/env python3
-"""Throughput benchmark: Kokoro decoder + generator (rokoko's hot path) on B200.
+"""Throughput benchmark: Kokoro-82M full pipeline (rokoko_infer: tokens + style
+-> PCM) on B200, BASELINE config 4, with the config-1 decoder as a nested record.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--batch 32] [--contexts 2] [--workload box|decoder]
 
-Workload: decoder/generator only, FP32 semantics, synthetic
-features asr [400, 512] ~ N(0,1), F0 [800] = 200 Hz +-50 Hz seeded walk,
-N [800] ~ N(0, 0.1), style [128] ~ N(0, 0.1), random-init weights in the KOKO
-v1 layout -> 240,000 samples = 10.0 s of 24 kHz audio per utterance.  A step is
-one utterance per GPU (independent utterances on every rank, no collective;
-weak scaling).  Metric: audio-seconds per second over all GPUs.
+Workload: 1024 utterances, token counts from a seeded
+truncated normal (mean 120, sd 60, clipped to [16, 510]) + BOS/EOS, durations
+U[2, 8] (the config's override), a seeded style vector each, FP16 weights (the
+KOKO v2 file written by rokoko_b200.convert_v2 from a seeded random-init v1
+file).  The utterances are sharded over the N ranks by rokoko_b200.shard
+(length buckets, greedy longest-processing-time; no collective in the data
+path).  A step is one batch of `batch` utterances of the rank's share: host
+token arrays -> rk_encode (the whole front half of the batch on the device,
+one duration read-back) -> rk_decode (decoder + generator per utterance) ->
+PCM in host memory.  Batches are dealt to `contexts` rk_ctx on the rank's GPU,
+each driven by its own host thread (one context's front half overlaps
+another's decode).  Per-GPU work per step is fixed (weak scaling); the steps
+visit the rank's batches in a fixed interleaved order that mixes short and
+long utterances, cycling when K exceeds the share.  Metric: audio-seconds
+produced per second over all GPUs.
 
-`value` is timed on the device with CUDA events on the library's stream,
-inputs resident in HBM; L2 is flushed (256 MB write) before every timed step,
-outside the events.  `e2e` is the same metric through the host-buffer C-ABI
-call rk_decode_features (pinned host inputs, host PCM out) timed with the
-wall clock.  `roofline` is the tcgen05 conv kernel measured live on a second
-pass of the same steps, replayed as a profiling CUDA graph with every lane on
-one stream, each conv launch bracketed by its own event nodes (the kernels'
-own time).  Under torchrun each rank
-drives LOCAL_RANK's GPU; ranks meet at a barrier and the max over ranks is
-reported by rank 0.
+`value`: K steps on every rank between a barrier + device synchronize on each
+side, timed with CUDA events (the step's token upload, front half, decode and
+PCM download included); max over ranks.  `e2e`: the same K steps plus the
+gather of every rank's PCM to rank 0 on the host (shard.gather_pcm), wall
+clock, max over ranks.  Before the timed steps every context runs one
+utterance of each decode-length bucket it will see (the predictor and decoder
+graphs are cached per bucket) and W warm-up steps.  The per-step working set
+(163 MB of FP16 weights plus the decode workspace) exceeds the 126 MB L2.
+
+`roofline` is the tcgen05 conv kernel, measured on rank 0 on the config-1
+decoder (L = 400, FP32 semantics): the decode replayed as a profiling CUDA
+graph with every lane on one stream, each conv launch bracketed by its own
+event nodes (the kernels' own time).  `decoder` nests the config-1 decode
+line of the earlier builds (device-timed graph replays with a 256 MB L2 flush
+before each, e2e through rk_decode_features with host buffers).
+`cpu_baseline` (rank 0, N = 1): the CPU restatement (oracle/) on a bounded
+sample of the same utterances, all host threads.
+
+`--impl reference` times the CPU restatement of the reference's path (its
+AVX2 CPU backend is not in its tree) on the box's host cores: each step is one
+config-4 utterance (FP16 weights semantics, tokens -> PCM) in the same
+interleaved order; rank 0 only.
 """
 from __future__ import annotations
 
@@ -35,12 +58,17 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# several rk_ctx per GPU, four streams each: give every stream its own hardware
+# work queue (the runtime's default of 8 would make unrelated streams wait on each other)
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
 
-L_FRAMES = 400
-AUDIO_S = 600 * L_FRAMES / 24000.0  # 10.0 s per utterance
 METRIC = "audio-sec/sec (RTF^-1)"
 UNIT = "audio-s/s"
-WORKLOAD = "config1: decoder+generator, L=400 frames -> 10.0 s of 24 kHz audio per utterance per GPU, FP32"
+SR = 24000.0
+L_DEC = 400
+WORKLOAD = ("config4: 1024 utterances, T ~ truncated N(120, 60) in [16, 510] + BOS/EOS, durations U[2,8], "
+            "seeded styles, FP16 weights; full pipeline tokens -> PCM, sharded over the ranks")
+WORKLOAD_DEC = "config1: decoder+generator, L=400 frames -> 10.0 s of 24 kHz audio per utterance per GPU, FP32"
 
 
 def parse_args():
@@ -49,6 +77,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--contexts", type=int, default=3)
+    p.add_argument("--workload", choices=["box", "decoder"], default="box")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -66,6 +97,12 @@ def measured_peaks():
             return json.load(f), "measured"
     except OSError:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def interleaved(n: int) -> list[int]:
+    """0..n-1 in a fixed order that alternates between the short and the long
+    end of a length-sorted list (golden-ratio stride)."""
+    return sorted(range(n), key=lambda i: ((i * 0.6180339887498949) % 1.0, i))
 
 
 # ------------------------------------------------------------------ clocks
@@ -122,46 +159,181 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU legs
-def cpu_oracle_throughput(blob, L: int, runs: int):
-    """Oracle (CPU restatement) decode of `runs` utterances of L frames, all host threads."""
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_box_sample(n_utt: int, fp16: bool = True):
+    """The CPU restatement (oracle/) running `n_utt` config-4 utterances
+    (tokens -> PCM, durations overridden as the config says) in the
+    interleaved order, all host threads.  Returns (audio-s/s, threads, seconds,
+    audio seconds)."""
     import oracle
-    from rokoko_b200 import configs
-    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    from rokoko_b200 import configs, koko, shard
+    threads = host_threads()
     oracle.set_threads(threads)
-    m = oracle.Oracle(blob)
-    c = configs.config1(seed=7, L=L)
+    utts = configs.config4(seed=0, count=1024)
+    order = shard.plan(shard.units(utts), 1)[0]
+    pick = [order[i] for i in interleaved(len(order))][:n_utt]
+    m = oracle.Oracle(koko.random_v1_blob(0), fp16=fp16)
+    audio = 0.0
     t0 = time.perf_counter()
-    for _ in range(runs):
-        m.decode_features(c.asr, c.f0, c.n, c.style)
+    for i in pick:
+        u = utts[i]
+        pcm, _, _, _ = m.infer(u.tokens, u.style, u.durations, bucket=32)
+        audio += pcm.shape[0] / SR
     dt = time.perf_counter() - t0
     m.close()
-    return runs * 600 * L / 24000.0 / dt, threads, dt
+    return audio / dt, threads, dt, audio
 
 
 def run_reference(args, world, rank):
-    """`--impl reference`: the CPU restatement of the reference's decoder path
-    (the reference's own CPU backend is absent from its tree), timed on this
-    box's host cores; rank 0 only."""
+    """`--impl reference`: the CPU restatement of the reference's path (the
+    reference's own CPU backend is absent from its tree), timed on this box's
+    host cores; rank 0 only.  Each step is one config-4 utterance."""
     if rank != 0:
         return
-    from rokoko_b200 import koko
-    blob = koko.random_v1_blob(0)
-    L = 100  # bounded per-step sample: 2.5 s of audio
-    for _ in range(args.warmup):
-        cpu_oracle_throughput(blob, L, 1)
-    v, threads, dt = cpu_oracle_throughput(blob, L, args.steps)
+    import oracle
+    from rokoko_b200 import configs, koko, shard
+    threads = host_threads()
+    oracle.set_threads(threads)
+    utts = configs.config4(seed=0, count=1024)
+    order = shard.plan(shard.units(utts), 1)[0]
+    seq = [order[i] for i in interleaved(len(order))]
+    m = oracle.Oracle(koko.random_v1_blob(0), fp16=True)
+
+    def step(k):
+        u = utts[seq[k % len(seq)]]
+        pcm, _, _, _ = m.infer(u.tokens, u.style, u.durations, bucket=32)
+        return pcm.shape[0] / SR
+
+    for k in range(args.warmup):
+        step(k)
+    audio = 0.0
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        audio += step(args.warmup + k)
+    dt = time.perf_counter() - t0
+    m.close()
+    v = audio / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": f"L={L} frames (2.5 s audio) per step",
+        "config": {"workload": WORKLOAD, "sample": f"one config-4 utterance per step ({audio:.1f} s of audio over "
+                                                    f"{args.steps} steps), FP16 weight semantics",
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} decodes of L={L} frames (CPU FP32 restatement; the reference "
-                                   "ships no CPU backend)"},
+                         "sample": f"{args.steps} config-4 utterances, tokens -> PCM (CPU restatement of "
+                                   "rokoko_infer; the reference ships no CPU backend)"},
         "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ decoder record (config 1)
+def decoder_record(dev, steps: int, warmup: int, flush):
+    """Config-1 decode (L = 400, FP32 semantics) on this GPU: device-timed graph
+    replays with an L2 flush before each, the conv roofline from a serial
+    profiling graph, e2e through rk_decode_features with host buffers."""
+    import torch
+    from rokoko_b200 import configs, koko
+    from rokoko_b200.context import FP32, RK_PROFILE_CONV, RK_PROFILE_SERIAL, Context
+    blob = koko.random_v1_blob(0)
+    ctx = Context(dev.index, FP32)
+    ctx.load_weights(blob)
+    c = configs.config1(seed=0, L=L_DEC)
+    d_asr = torch.from_numpy(c.asr).to(dev)
+    d_f0 = torch.from_numpy(c.f0).to(dev)
+    d_n = torch.from_numpy(c.n).to(dev)
+    d_st = torch.from_numpy(c.style).to(dev)
+    d_pcm = torch.empty(600 * L_DEC, dtype=torch.float32, device=dev)
+    ext = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    audio_s = 600 * L_DEC / SR
+
+    def step():
+        ctx.decode_features_device(d_asr.data_ptr(), d_f0.data_ptr(), d_n.data_ptr(), d_st.data_ptr(), L_DEC,
+                                   d_pcm.data_ptr())
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    k0 = ctx.kernel_count()
+    with torch.cuda.stream(ext):
+        for k in range(steps):
+            flush.zero_()
+            ev0[k].record(ext)
+            step()
+            ev1[k].record(ext)
+    torch.cuda.synchronize(dev)
+    launches = ctx.kernel_count() - k0
+    t_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1))
+    # conv roofline: a profiling graph with every lane on the context stream; each conv
+    # launch bracketed by its own pair of event nodes and alone on the GPU
+    ctx.profile(RK_PROFILE_CONV | RK_PROFILE_SERIAL)
+    step()
+    ctx.profile_read()
+    ctx.profile(RK_PROFILE_CONV | RK_PROFILE_SERIAL)
+    torch.cuda.synchronize(dev)
+    serial_ms = 0.0
+    ps0, ps1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(ext):
+        for k in range(steps):
+            flush.zero_()
+            ps0.record(ext)
+            step()
+            ps1.record(ext)
+            ctx.profile_read()
+            serial_ms += ps0.elapsed_time(ps1)
+    conv_ms, conv_flops, conv_n = ctx.profile_read()
+    ctx.profile(False)
+    # end to end through the host-buffer call
+    h = [torch.from_numpy(a).pin_memory().numpy() for a in (c.asr, c.f0, c.n, c.style)]
+    for _ in range(2):
+        ctx.decode_features(*h)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        pcm = ctx.decode_features(*h)
+    e2e_s = time.perf_counter() - t0
+    ctx.close()
+    return {
+        "workload": WORKLOAD_DEC, "value": round(audio_s * steps / (t_ms / 1000.0), 2), "unit": UNIT,
+        "ms_per_step": round(t_ms / steps, 4), "steps": steps, "launches_per_step": launches / steps,
+        "precision": "FP32 semantics: 3-pass split-bf16 tcgen05 products, FP32 accumulate",
+        "l2": "256 MB L2 flush before every timed step (outside the events)",
+        "e2e": {"value": round(audio_s * steps / e2e_s, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(sum(a.nbytes for a in (c.asr, c.f0, c.n, c.style))),
+                "d2h_bytes_per_step": int(pcm.nbytes)},
+        "_conv": (conv_ms / steps, conv_flops / steps, conv_n, serial_ms / steps, t_ms / steps),
+    }
+
+
+def roofline_from(dec, peaks, src):
+    conv_ms, conv_flops, conv_n, serial_ms, step_ms = dec.pop("_conv")
+    peak = float(peaks.get("bf16_tflops"))
+    achieved = conv_flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else 0.0
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "conv_tc_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    return {
+        "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM Conv1d / ConvTranspose1d)",
+        "bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+        "frac": round(achieved / peak, 4), "traffic": traffic,
+        "traffic_source": "copied from profiles/conv_tc_traffic.json (one ncu capture), not measured in this run",
+        "peak_source": f"bf16_tflops (burst) of {src}: each conv launch is timed alone between its own events",
+        "flops": "algorithmic 2*C_in*C_out*K*T_out per conv (x T_in for ConvTranspose1d); the FP32 semantics "
+                 "issue 3 bf16 products per algorithmic product",
+        "issued_frac": round(3 * achieved / peak, 4),
+        "conv_launches_per_step": conv_n, "conv_ms_per_step": round(conv_ms, 4),
+        "serial_step_ms": round(serial_ms, 4),
+        "conv_share_of_serial_step": round(conv_ms / serial_ms, 4) if serial_ms > 0 else None,
+        "step_ms": round(step_ms, 4),
+        "workload": "config-1 decoder (L = 400, FP32 semantics) on rank 0",
+    }
 
 
 # ------------------------------------------------------------------ GPU leg
@@ -169,13 +341,15 @@ def run_ours(args, world, rank, local):
     import numpy as np
     import torch
     import torch.distributed as dist
-    from rokoko_b200 import configs, koko
-    from rokoko_b200.context import FP32, RK_PROFILE_CONV, RK_PROFILE_SERIAL, Context
+    from rokoko_b200 import boxbench, configs, convert_v2, koko, shard
+    from rokoko_b200.context import FP16, Context
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    host_group = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
 
     def barrier():
         if world > 1:
@@ -188,138 +362,177 @@ def run_ours(args, world, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    blob = koko.random_v1_blob(0)
-    ctx = Context(local, FP32)
-    ctx.load_weights(blob)
-    c = configs.config1(seed=rank, L=L_FRAMES)
-    d_asr = torch.from_numpy(c.asr).to(dev)
-    d_f0 = torch.from_numpy(c.f0).to(dev)
-    d_n = torch.from_numpy(c.n).to(dev)
-    d_st = torch.from_numpy(c.style).to(dev)
-    d_pcm = torch.empty(600 * L_FRAMES, dtype=torch.float32, device=dev)
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
-    ext = torch.cuda.ExternalStream(ctx.stream, device=dev)
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
 
-    def step():
-        ctx.decode_features_device(d_asr.data_ptr(), d_f0.data_ptr(), d_n.data_ptr(), d_st.data_ptr(), L_FRAMES,
-                                   d_pcm.data_ptr())
+    # ---- the workload: config 4 sharded over the ranks; every rank computes the same plan
+    utts = configs.config4(seed=0, count=1024)
+    items = shard.units(utts)
+    plan = shard.plan(items, world)
 
+    def rank_steps(r):
+        share = plan[r]
+        batches = [share[k:k + args.batch] for k in range(0, len(share), args.batch)]
+        order = interleaved(len(batches))
+        return [batches[order[k % len(batches)]] for k in range(args.warmup + args.steps)]
+
+    all_steps = [rank_steps(r) for r in range(world)]
+    mine = all_steps[rank]
+    warm, timed = mine[:args.warmup], mine[args.warmup:]
+
+    blob = convert_v2.convert_blob(koko.random_v1_blob(0))
+    ctxs = [Context(local, FP16) for _ in range(max(1, args.contexts))]
+    for ctx in ctxs:
+        ctx.load_weights(blob)
+    # graph warm-up: every context runs one utterance of each decode-length bucket it will see
+    # (largest first, so each workspace is sized once)
+    first = {}
+    for b in mine:
+        for i in b:
+            first.setdefault(items[i].L_b, i)
+    wl = [first[k] for k in sorted(first, reverse=True)]
+    for ctx in ctxs:
+        for k in range(0, len(wl), args.batch):
+            _, Ls = ctx.encode([utts[i] for i in wl[k:k + args.batch]])
+            ctx.decode(Ls)
+    boxbench.run_batches(ctxs, utts, warm)
     torch.cuda.synchronize(dev)
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    # ---- timed region: K steps
     clocks = ClockSampler(local)
-
-    # ---- timed region: graph replays, device events around every step
-    k0 = ctx.kernel_count()
+    k0 = sum(ctx.kernel_count() for ctx in ctxs)
     barrier()
     torch.cuda.synchronize(dev)
     clocks.start()
-    with torch.cuda.stream(ext):
-        for k in range(args.steps):
-            flush.zero_()
-            ev0[k].record(ext)
-            step()
-            ev1[k].record(ext)
-    torch.cuda.synchronize(dev)
-    barrier()
-    clk = clocks.stop()
-    launches = ctx.kernel_count() - k0
-    t_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1))
-    t_ms = max_over_ranks(t_ms)
-    value = world * AUDIO_S * args.steps / (t_ms / 1000.0)
-
-    # ---- conv roofline: the same K steps again as a profiling graph with every lane on
-    # the context stream (RK_PROFILE_CONV | RK_PROFILE_SERIAL), so each conv launch is
-    # bracketed by its own pair of event nodes and runs alone on the GPU; the graph's
-    # total device time gives the conv share of a serialised decode
-    ctx.profile(RK_PROFILE_CONV | RK_PROFILE_SERIAL)
-    step()
-    ctx.profile_read()
-    ctx.profile(RK_PROFILE_CONV | RK_PROFILE_SERIAL)
-    torch.cuda.synchronize(dev)
-    serial_ms = 0.0
-    ps0, ps1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(ext):
-        for k in range(args.steps):
-            flush.zero_()
-            ps0.record(ext)
-            step()
-            ps1.record(ext)
-            ctx.profile_read()  # synchronises; the next replay re-records the same event nodes
-            serial_ms += ps0.elapsed_time(ps1)
-    conv_ms, conv_flops, conv_n = ctx.profile_read()
-    ctx.profile(False)
-
-    # ---- end to end through the host-buffer API (pinned inputs, host PCM)
-    h_asr = torch.from_numpy(c.asr).pin_memory().numpy()
-    h_f0 = torch.from_numpy(c.f0).pin_memory().numpy()
-    h_n = torch.from_numpy(c.n).pin_memory().numpy()
-    h_st = torch.from_numpy(c.style).pin_memory().numpy()
-    for _ in range(2):
-        ctx.decode_features(h_asr, h_f0, h_n, h_st)
-    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    phase = []
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        pcm = ctx.decode_features(h_asr, h_f0, h_n, h_st)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    ev0.record()
+    local_pcm = boxbench.run_batches(ctxs, utts, timed, phase)
+    torch.cuda.synchronize(dev)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    t_rank = time.perf_counter() - t0
+    clk = clocks.stop()
     barrier()
-    e2e = world * AUDIO_S * args.steps / e2e_s
-    h2d = c.asr.nbytes + c.f0.nbytes + c.n.nbytes + c.style.nbytes
-    d2h = pcm.nbytes
+    launches = sum(ctx.kernel_count() for ctx in ctxs) - k0
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    audio_local = sum(p.shape[0] for _, p in local_pcm) / SR
+    audio_all = sum_over_ranks(audio_local)
+
+    # ---- e2e: the same steps' PCM gathered to rank 0 on the host (unique slot per (rank, step, item))
+    offs, acc = [], 0
+    for r in range(world):
+        offs.append(acc)
+        acc += sum(len(b) for b in all_steps[r][args.warmup:])
+    n_slots = acc
+    slot_of = {}
+    k = offs[rank]
+    for b in timed:
+        for i in b:
+            slot_of.setdefault(i, []).append(k)
+            k += 1
+    keyed = []
+    for i, pcm in local_pcm:
+        keyed.append((slot_of[i].pop(0), pcm))
+    tg = time.perf_counter()
+    gathered = shard.gather_pcm(keyed, n_slots, group=host_group)
+    t_gather = time.perf_counter() - tg
+    t_e2e = max_over_ranks(t_rank + t_gather)
+
+    # per-step host <-> device bytes (rank 0's timed steps): tokens, T, styles, durations in;
+    # durations, L and PCM out
+    h2d = sum(sum(4 * (2 * utts[i].tokens.shape[0] + 1 + 256) for i in b) for b in timed) / len(timed)
+    d2h = sum(sum(4 * (utts[i].tokens.shape[0] + 1) + 4 * 600 * int(utts[i].durations.sum()) for i in b)
+              for b in timed) / len(timed)
+
+    decoder = None
+    if rank == 0:
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
+        decoder = decoder_record(dev, max(3, min(args.steps, 20)), max(3, args.warmup), flush)
+        del flush
+    for ctx in ctxs:
+        ctx.close()
 
     if rank == 0:
+        samples_ok = None
+        if gathered is not None:
+            expect = []
+            for r in range(world):
+                for b in all_steps[r][args.warmup:]:
+                    expect.extend(600 * int(utts[i].durations.sum()) for i in b)
+            samples_ok = [p.shape[0] for p in gathered] == expect
         peaks, src = measured_peaks()
-        peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-        achieved = conv_flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else 0.0
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "conv_tc_traffic.json")
-        if os.path.exists(tp):
-            with open(tp) as f:
-                traffic = json.load(f).get("dram_bytes_per_launch")
+        roof = roofline_from(decoder, peaks, src)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            v, threads, dt = cpu_oracle_throughput(blob, L_FRAMES, 2)
+            v, threads, dt, aud = cpu_box_sample(2)
             cpu = {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"2 decodes of the config-1 utterance (L={L_FRAMES}, 20 s of audio, {dt:.1f} s of "
-                             "CPU work) with the CPU FP32 restatement; the reference ships no CPU backend"}
+                   "sample": f"2 config-4 utterances in the steps' order ({aud:.1f} s of audio, {dt:.1f} s of CPU "
+                             "work), tokens -> PCM, CPU restatement in FP16 weight semantics; the reference ships "
+                             "no CPU backend"}
+        value = audio_all / (dev_ms / 1000.0)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {
-                "workload": WORKLOAD, "L": L_FRAMES, "audio_s_per_step_per_gpu": AUDIO_S,
-                "precision": "FP32 semantics: 3-pass split-bf16 tcgen05 products, FP32 accumulate",
-                "parallelism": f"dp{world} (independent utterances per GPU, no collective)",
-                "l2": "256 MB L2 flush before every timed step (outside the events); per-step working set > L2",
-                "launches_per_step": launches / args.steps,
+                "workload": WORKLOAD, "utterances_per_step_per_gpu": args.batch,
+                "audio_s_timed": round(audio_all, 1),
+                "precision": "FP16 weights (KOKO v2), fp16 tensor-core products, FP32 accumulate",
+                "parallelism": f"dp{world}: utterances sharded by length bucket (shard.plan), no collective; "
+                               f"{len(ctxs)} rk_ctx per GPU on host threads",
+                "l2": "no flush: per-step working set (163 MB FP16 weights + decode workspace) > 126 MB L2",
+                "value_timing": "CUDA events around the K steps after a device sync (token upload, front half, "
+                                "decode, PCM download to host included; PCM gather excluded); max over ranks",
+                "pcm_gathered_on_rank0": samples_ok,
+                "rank0_host_s": {"steps_wall": round(t_rank, 3), "gather": round(t_gather, 3),
+                                 "encode_per_ctx": [round(p[0], 3) for p in phase],
+                                 "decode_per_ctx": [round(p[1], 3) for p in phase]},
             },
             "clocks": clk,
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": round(audio_all / t_e2e, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h),
+                    "timing": "wall clock of the K steps (host tokens in, host PCM out) plus the host gather of "
+                              "every rank's PCM to rank 0, max over ranks"},
             "gpu_launches": launches,
-            "roofline": {
-                "kernel": "conv_tc_kernel (tcgen05 implicit-GEMM Conv1d / ConvTranspose1d)",
-                "bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
-                "peak_source": f"bf16_tflops_sustained of {src}",
-                "flops": "algorithmic 2*C_in*C_out*K*T_out per conv (x T_in for ConvTranspose1d); the FP32 "
-                         "semantics issue 3 bf16 products per algorithmic product",
-                "issued_frac": round(3 * achieved / peak, 4),
-                "conv_launches": conv_n, "conv_ms_per_step": round(conv_ms / args.steps, 4),
-                "serial_step_ms": round(serial_ms / args.steps, 4),
-                "conv_share_of_serial_step": round(conv_ms / serial_ms, 4) if serial_ms > 0 else None,
-                "step_ms": round(t_ms / args.steps, 4),
-                "measured": "second pass of the same K steps as a CUDA graph with all lanes on one stream; each conv "
-                            "launch bracketed by its own event nodes (kernel time alone on the GPU); issued_frac counts "
-                            "the 3 bf16 products per algorithmic product of the FP32 semantics",
-            },
+            "roofline": roof,
             "cpu_baseline": cpu,
+            "decoder": decoder,
         }
         print(json.dumps(line), flush=True)
-    ctx.close()
     if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_decoder_only(args, world, rank, local):
+    """--workload decoder: the config-1 decode line alone (one utterance per GPU per step)."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    if world > 1:
+        dist.barrier()
+    dec = decoder_record(dev, args.steps, args.warmup, flush)
+    if rank == 0:
+        peaks, src = measured_peaks()
+        roof = roofline_from(dec, peaks, src)
+        line = {"metric": METRIC, "value": dec["value"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": dec["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD_DEC, "note": "rank 0's GPU only"}, "e2e": dec["e2e"],
+                "roofline": roof}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -328,6 +541,8 @@ def main():
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
+    elif args.workload == "decoder":
+        run_decoder_only(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 

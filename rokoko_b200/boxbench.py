@@ -50,8 +50,14 @@ def run_share(ctxs, utts, indices, batch: int, timings=None):
     `ctxs` (all on this rank's GPU), each context driven by its own host
     thread.  Returns [(index, PCM)] (context by context); `timings`, if given,
     receives [encode_s, decode_s] per context."""
-    import threading
     batches = [indices[k:k + batch] for k in range(0, len(indices), batch)]
+    return run_batches(ctxs, utts, batches, timings)
+
+
+def run_batches(ctxs, utts, batches, timings=None):
+    """run_share over explicit batches (lists of indices into `utts`): batch k
+    goes to context k % len(ctxs)."""
+    import threading
     per_ctx = [batches[c::len(ctxs)] for c in range(len(ctxs))]
     results = [[] for _ in ctxs]
     tim = [[0.0, 0.0] for _ in ctxs]

@@ -14,9 +14,9 @@ file).  The utterances are sharded over the N ranks by rokoko_b200.shard
 path).  A step is one batch of `batch` utterances of the rank's share: host
 token arrays -> rk_encode (the whole front half of the batch on the device,
 one duration read-back) -> rk_decode (decoder + generator per utterance) ->
-PCM in host memory.  Batches are dealt to `contexts` rk_ctx on the rank's GPU,
-each driven by its own host thread (one context's front half overlaps
-another's decode).  Per-GPU work per step is fixed (weak scaling); the steps
+PCM in host memory.  Batches are taken from a shared queue by `contexts`
+rk_ctx on the rank's GPU, each driven by its own host thread (one context's
+front half overlaps another's decode).  Per-GPU work per step is fixed (weak scaling); the steps
 visit the rank's batches in a fixed interleaved order that mixes short and
 long utterances, cycling when K exceeds the share.  Metric: audio-seconds
 produced per second over all GPUs.
@@ -420,7 +420,9 @@ def run_ours(args, world, rank, local):
     clk = clocks.stop()
     barrier()
     launches = sum(ctx.kernel_count() for ctx in ctxs) - k0
-    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    my_ms = ev0.elapsed_time(ev1)
+    dev_ms = max_over_ranks(my_ms)
+    min_ms = -max_over_ranks(-my_ms)
     audio_local = sum(p.shape[0] for _, p in local_pcm) / SR
     audio_all = sum_over_ranks(audio_local)
 
@@ -490,6 +492,7 @@ def run_ours(args, world, rank, local):
                 "value_timing": "CUDA events around the K steps after a device sync (token upload, front half, "
                                 "decode, PCM download to host included; PCM gather excluded); max over ranks",
                 "pcm_gathered_on_rank0": samples_ok,
+                "rank_device_s": {"max": round(dev_ms / 1000, 3), "min": round(min_ms / 1000, 3)},
                 "rank0_host_s": {"steps_wall": round(t_rank, 3), "gather": round(t_gather, 3),
                                  "encode_per_ctx": [round(p[0], 3) for p in phase],
                                  "decode_per_ctx": [round(p[1], 3) for p in phase]},

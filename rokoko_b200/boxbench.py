@@ -9,8 +9,8 @@ vector each (configs.config4), FP16 weights (the KOKO v2 file) unless --fp32.
 The utterances are sharded over the ranks by rokoko_b200.shard (length
 buckets, greedy longest-processing-time; no collective in the data path);
 each rank runs its share through rk_encode + rk_decode in batches of `batch`
-utterances in the plan's bucket order, dealt round-robin to `contexts` rk_ctx
-on the same GPU, each driven by its own host thread, so that one context's
+utterances in the plan's bucket order, taken from a shared queue by `contexts`
+rk_ctx on the same GPU, each driven by its own host thread, so that one context's
 latency-bound front half (ALBERT, BiLSTM recurrences) overlaps another's
 SM-saturating decode; rank 0 gathers the PCM on the host (ranks on one host
 write it into one shared node-local file, rokoko_b200.shard.gather_pcm).
@@ -46,26 +46,40 @@ def _args(argv=None):
 
 def run_share(ctxs, utts, indices, batch: int, timings=None):
     """This rank's share `indices` of `utts` through rk_encode + rk_decode in
-    batches of `batch` (in the given order), dealt round-robin to the contexts
-    `ctxs` (all on this rank's GPU), each context driven by its own host
-    thread.  Returns [(index, PCM)] (context by context); `timings`, if given,
+    batches of `batch` (in the given order), taken from a shared queue by the
+    contexts `ctxs` (all on this rank's GPU), each context driven by its own
+    host thread.  Returns [(index, PCM)] (context by context); `timings`, if given,
     receives [encode_s, decode_s] per context."""
     batches = [indices[k:k + batch] for k in range(0, len(indices), batch)]
     return run_batches(ctxs, utts, batches, timings)
 
 
 def run_batches(ctxs, utts, batches, timings=None):
-    """run_share over explicit batches (lists of indices into `utts`): batch k
-    goes to context k % len(ctxs)."""
+    """run_share over explicit batches (lists of indices into `utts`): every
+    context's host thread takes the next batch not yet taken, so a context that
+    drew short utterances takes more batches (the outputs do not depend on
+    which context runs a batch)."""
     import threading
-    per_ctx = [batches[c::len(ctxs)] for c in range(len(ctxs))]
     results = [[] for _ in ctxs]
     tim = [[0.0, 0.0] for _ in ctxs]
     errors = []
+    lock = threading.Lock()
+    nxt = [0]
+
+    def take():
+        with lock:
+            if errors or nxt[0] >= len(batches):
+                return None
+            b = batches[nxt[0]]
+            nxt[0] += 1
+            return b
 
     def worker(c: int) -> None:
         try:
-            for idx in per_ctx[c]:
+            while True:
+                idx = take()
+                if idx is None:
+                    return
                 te = time.perf_counter()
                 _, Ls = ctxs[c].encode([utts[i] for i in idx])
                 td = time.perf_counter()
@@ -74,7 +88,8 @@ def run_batches(ctxs, utts, batches, timings=None):
                 tim[c][1] += time.perf_counter() - td
                 results[c].extend(zip(idx, pcms))
         except BaseException as e:  # re-raised after the join
-            errors.append(e)
+            with lock:
+                errors.append(e)
 
     threads = [threading.Thread(target=worker, args=(c,)) for c in range(len(ctxs))]
     for th in threads:
@@ -117,19 +132,14 @@ def main(argv=None) -> int:
     for ctx in ctxs:
         ctx.load_weights(blob)
 
-    # batches of this rank's share (plan order), dealt round-robin to the contexts
-    batches = [mine[k:k + a.batch] for k in range(0, len(mine), a.batch)]
-    per_ctx = [batches[c::len(ctxs)] for c in range(len(ctxs))]
-
     # warm-up outside the timed pass: one utterance of every decode-length bucket
-    # each context will see (the decode graphs are cached per bucket), largest
-    # first so that the decode workspace is sized once
-    for ctx, bl in zip(ctxs, per_ctx):
-        first = {}
-        for b in bl:
-            for i in b:
-                first.setdefault(items[i].L_b, i)
-        warm = [first[k] for k in sorted(first, reverse=True)]
+    # of this rank's share on every context (the predictor and decode graphs are
+    # cached per bucket), largest first so that the decode workspace is sized once
+    first = {}
+    for i in mine:
+        first.setdefault(items[i].L_b, i)
+    warm = [first[k] for k in sorted(first, reverse=True)]
+    for ctx in ctxs:
         for k in range(0, len(warm), a.batch):
             _, Ls = ctx.encode([utts[i] for i in warm[k:k + a.batch]])
             ctx.decode(Ls)

@@ -4,7 +4,9 @@
 
 Every translation unit under rokoko_b200/csrc is compiled with
 `-gencode arch=compute_100a,code=sm_100a -lineinfo -O3` and linked into one
-shared library (static cudart, no cuBLAS/cuDNN/CUTLASS).  Objects are cached in
+shared library (static cudart, no cuBLAS/cuDNN/CUTLASS).  The C++ model seam
+of the reference (rokoko_b200/cpp, include/rokoko/weights.h) is compiled with
+g++ into librokoko_compat.so on top of it.  Objects are cached in
 rokoko_b200/_build and rebuilt when a source or header is newer.
 """
 from __future__ import annotations
@@ -19,6 +21,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "librokoko_b200.so")
+COMPAT = os.path.join(HERE, "librokoko_compat.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -68,7 +71,26 @@ def build(force: bool = False, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stdout + r.stderr)
+    build_compat(force)
     return LIB
+
+
+def build_compat(force: bool = False) -> str:
+    """librokoko_compat.so: the reference's C++ model seam (include/rokoko/weights.h)
+    on top of librokoko_b200.so, compiled with the system g++."""
+    src = os.path.join(HERE, "cpp", "rokoko_compat.cpp")
+    hdrs = [os.path.join(INCLUDE, "rokoko", "weights.h"), os.path.join(INCLUDE, "rk_b200.h")]
+    if not force and not _stale(COMPAT, [src, LIB] + hdrs):
+        return COMPAT
+    cuda = os.path.dirname(os.path.dirname(NVCC))
+    cmd = ["/usr/bin/g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-I", os.path.join(INCLUDE, "rokoko"),
+           "-I", os.path.join(cuda, "include"), src, "-o", COMPAT, "-L", HERE, "-lrokoko_b200",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart_static", "-ldl", "-lpthread", "-lrt",
+           "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("compat library build failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
+    return COMPAT
 
 
 if __name__ == "__main__":

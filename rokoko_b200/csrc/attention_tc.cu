@@ -1,0 +1,313 @@
+// attention_tc.cu -- ALBERT self-attention on the tensor cores (tcgen05 / TMEM).
+//
+// Reference: src/rokoko_f16.cpp:227-244 (batched GEMM Q K^T, softmax kernel
+// src/kernels.cu:189-225, batched GEMM P V) and src/rokoko.cpp:363-384:
+// S = Q K^T * 0.125 over 12 heads of 64, softmax over the keys (no mask),
+// O = P V, for every utterance of the batch (segments of the row layout).
+//
+// One CTA of 128 threads per (128-query tile, head, utterance):
+//   1. Q [128 x 64] and, in chunks of 64 keys, K [64 x 64] are converted from
+//      the FP32 QKV rows into 16-bit planes in shared memory (the 128-byte
+//      swizzled K-major layout the MMA reads; FP32 semantics keep bf16 hi and
+//      lo planes and issue hi*hi + hi*lo + lo*hi), and one elected thread
+//      issues S[:, 64c .. 64c+64) = Q K_c^T into TMEM (M = 128 queries,
+//      N = 64 keys, K = 64 dims), chunks double-buffered behind mbarriers.
+//   2. Thread i owns query row i = TMEM lane i: it reads its scores straight
+//      from TMEM (tcgen05.ld), takes the row maximum, then per key chunk
+//      computes e = exp(0.125 s - max) (0 past the utterance's keys), adds it
+//      to the row sum and writes the row of E_c into shared memory; V_c is
+//      written transposed (dims x keys) beside it; the elected thread issues
+//      O += E_c V_c into TMEM columns 0..63 (the columns of chunk 0's scores,
+//      read before the first such MMA).
+//   3. O row / sum -> ctx.
+// The scores never leave the SM.  Every wait is bounded (ptx.cuh): a timeout
+// records an error code in the context's error word and the CTA finishes
+// without writing (the host reports RK_ERR_DEVICE_TIMEOUT).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "front_ops.cuh"
+#include "ptx.cuh"
+
+namespace rk {
+
+namespace {
+
+constexpr int QT = 128;   // queries per CTA (the MMA M)
+constexpr int KC = 64;    // keys per chunk (the S MMA N, the O MMA K)
+constexpr int HD = 64;    // head dim
+constexpr uint32_t ROWB = 128;  // bytes per 64-element 16-bit row
+
+template <bool SPLIT>
+struct AttCfg {
+    static constexpr int NPL = SPLIT ? 2 : 1;
+    static constexpr uint32_t Q_PLANE = QT * ROWB;    // 16 KB
+    static constexpr uint32_t K_PLANE = KC * ROWB;    // 8 KB
+    static constexpr uint32_t E_PLANE = QT * ROWB;    // 16 KB
+    static constexpr uint32_t V_PLANE = HD * ROWB;    // 8 KB
+    static constexpr uint32_t Q_OFF = 0;
+    static constexpr uint32_t K_OFF = Q_OFF + NPL * Q_PLANE;          // 2 buffers
+    static constexpr uint32_t E_OFF = K_OFF + 2 * NPL * K_PLANE;      // 2 buffers
+    static constexpr uint32_t V_OFF = E_OFF + 2 * NPL * E_PLANE;      // 2 buffers
+    static constexpr uint32_t BYTES = V_OFF + 2 * NPL * V_PLANE;
+};
+
+// byte offset of 16-bit element (r, k) of a [rows][64] tile in the 128-byte swizzle
+__device__ __forceinline__ uint32_t sw_off(int r, int k) {
+    return (uint32_t)r * ROWB + ((((uint32_t)k >> 3) ^ ((uint32_t)r & 7u)) << 4) + (((uint32_t)k & 7u) << 1);
+}
+
+// 8 FP32 values -> one 16-byte chunk of the hi plane (and the lo plane when split)
+template <bool SPLIT>
+__device__ __forceinline__ void put8(uint8_t* hi, uint8_t* lo, uint32_t off, const float (&v)[8]) {
+    if (SPLIT) {
+        __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            h[j] = __float2bfloat16_rn(v[j]);
+            l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+        }
+        *reinterpret_cast<uint4*>(hi + off) = *reinterpret_cast<uint4*>(h);
+        *reinterpret_cast<uint4*>(lo + off) = *reinterpret_cast<uint4*>(l);
+    } else {
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) h[j] = __float2half_rn(v[j]);
+        *reinterpret_cast<uint4*>(hi + off) = *reinterpret_cast<uint4*>(h);
+    }
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// D (+)= A B^T over one 64-wide K block: 4 MMAs of K = 16 (x3 products when split)
+template <bool SPLIT>
+__device__ __forceinline__ void mma_block(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                          uint32_t b_lo, uint32_t idesc, bool accumulate) {
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+        const uint64_t ah = sw128_kmajor_desc(a_hi + kk * 32, 0), bh = sw128_kmajor_desc(b_hi + kk * 32, 0);
+        umma_f16(d_tmem, ah, bh, idesc, (accumulate || kk > 0) ? 1u : 0u);
+        if (SPLIT) {
+            umma_f16(d_tmem, ah, sw128_kmajor_desc(b_lo + kk * 32, 0), idesc, 1u);
+            umma_f16(d_tmem, sw128_kmajor_desc(a_lo + kk * 32, 0), bh, idesc, 1u);
+        }
+    }
+}
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restrict__ qkv_all, SegMeta s,
+                                                           float* __restrict__ ctx_all, uint32_t* err) {
+    using C = AttCfg<SPLIT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t s_bar[2], pv_bar[2], fin_bar;
+    __shared__ uint32_t tmem_base_sh;
+
+    const int T = s.len[blockIdx.z];
+    const int q0 = blockIdx.x * QT;
+    if (q0 >= T) return;  // uniform over the CTA
+    const int head = blockIdx.y;
+    const float* qkv = qkv_all + (size_t)s.off[blockIdx.z] * 2304;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int nch = (T + KC - 1) / KC;
+    uint32_t ncols = 64;
+    while ((int)ncols < nch * KC) ncols <<= 1;
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) { mbar_init(&s_bar[i], 1); mbar_init(&pv_bar[i], 1); }
+        mbar_init(&fin_bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&tmem_base_sh, ncols);
+        tmem_relinquish();
+    }
+    // ---- Q tile: thread t = query row q0 + t (zeros past T)
+    {
+        uint8_t* qh = smem + C::Q_OFF;
+        uint8_t* ql = qh + C::Q_PLANE;
+        const int q = q0 + tid;
+        const float* src = qkv + (size_t)q * 2304 + head * HD;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float v[8];
+            if (q < T) {
+                const float4 a = reinterpret_cast<const float4*>(src + 8 * j)[0];
+                const float4 b = reinterpret_cast<const float4*>(src + 8 * j)[1];
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = 0.f;
+            }
+            put8<SPLIT>(qh, ql, sw_off(tid, 8 * j), v);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const uint32_t idesc = umma_idesc_f16(QT, KC, SPLIT);
+    const uint32_t q_hi = smem_u32(smem + C::Q_OFF), q_lo = q_hi + C::Q_PLANE;
+    bool ok = true;
+
+    // ---- phase S: scores of every key chunk into TMEM columns [64c, 64c + 64)
+    for (int c = 0; c < nch; c++) {
+        const int buf = c & 1;
+        if (c >= 2 && !mbar_wait(&s_bar[buf], ((c - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+        if (!__syncthreads_and(ok)) break;
+        uint8_t* kh = smem + C::K_OFF + buf * C::NPL * C::K_PLANE;
+        uint8_t* kl = kh + C::K_PLANE;
+        {   // key row t >> 1, dims [32 (t & 1), +32)
+            const int kr = tid >> 1, half = tid & 1;
+            const int key = c * KC + kr;
+            const float* src = qkv + (size_t)key * 2304 + 768 + head * HD + 32 * half;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float v[8];
+                if (key < T) {
+                    const float4 a = reinterpret_cast<const float4*>(src + 8 * j)[0];
+                    const float4 b = reinterpret_cast<const float4*>(src + 8 * j)[1];
+                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = 0.f;
+                }
+                put8<SPLIT>(kh, kl, sw_off(kr, 32 * half + 8 * j), v);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t k_hi = smem_u32(kh), k_lo = k_hi + C::K_PLANE;
+            mma_block<SPLIT>(tmem + (uint32_t)(c * KC), q_hi, q_lo, k_hi, k_lo, idesc, false);
+            umma_commit(&s_bar[buf]);
+        }
+    }
+    if (tid == 0 && ok) umma_commit(&fin_bar);
+    if (ok && !mbar_wait(&fin_bar, 0, err, RK_DEV_TIMEOUT_ACC)) ok = false;
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+
+    const uint32_t row_tmem = tmem + ((uint32_t)(warp * 32) << 16);
+    float mx = -3.0e38f, sum = 0.f;
+    if (ok) {
+        // ---- pass A: row maximum of the scaled scores over the utterance's keys
+        for (int c = 0; c < nch; c++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float v[32];
+                tmem_ld32(row_tmem + (uint32_t)(c * KC + 32 * h), v);
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if (c * KC + 32 * h + j < T) mx = fmaxf(mx, v[j] * 0.125f);
+            }
+        }
+        // ---- pass B: e = exp(0.125 s - max) chunk by chunk, O += E_c V_c
+        for (int c = 0; c < nch; c++) {
+            const int buf = c & 1;
+            if (c >= 2 && !mbar_wait(&pv_bar[buf], ((c - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+            if (!__syncthreads_and(ok)) break;
+            uint8_t* eh = smem + C::E_OFF + buf * C::NPL * C::E_PLANE;
+            uint8_t* el = eh + C::E_PLANE;
+            uint8_t* vh = smem + C::V_OFF + buf * C::NPL * C::V_PLANE;
+            uint8_t* vl = vh + C::V_PLANE;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float v[32];
+                tmem_ld32(row_tmem + (uint32_t)(c * KC + 32 * h), v);
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const float e = (c * KC + 32 * h + j < T) ? expf(v[j] * 0.125f - mx) : 0.f;
+                    sum += e;
+                    v[j] = e;
+                }
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+                    float w[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) w[i] = v[8 * g + i];
+                    put8<SPLIT>(eh, el, sw_off(tid, 32 * h + 8 * g), w);
+                }
+            }
+            {   // V_c transposed: thread t -> dim t & 63, keys 32 (t >> 6) .. +32 in chunks of 8
+                const int d = tid & 63, kh0 = (tid >> 6) * 32;
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+                    float w[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int key = c * KC + kh0 + 8 * g + i;
+                        w[i] = key < T ? qkv[(size_t)key * 2304 + 1536 + head * HD + d] : 0.f;
+                    }
+                    put8<SPLIT>(vh, vl, sw_off(d, kh0 + 8 * g), w);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t e_hi = smem_u32(eh), e_lo = e_hi + C::E_PLANE;
+                const uint32_t v_hi = smem_u32(vh), v_lo = v_hi + C::V_PLANE;
+                mma_block<SPLIT>(tmem, e_hi, e_lo, v_hi, v_lo, idesc, c > 0);
+                umma_commit(&pv_bar[buf]);
+            }
+        }
+    }
+    if (tid == 0 && ok) umma_commit(&fin_bar);
+    if (ok && !mbar_wait(&fin_bar, 1, err, RK_DEV_TIMEOUT_ACC)) ok = false;
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (ok) {
+        // ---- O / sum -> ctx (row q0 + t, columns head*64 ..)
+        const int q = q0 + tid;
+        const float inv = 1.0f / sum;
+        float* dst = ctx_all + ((size_t)s.off[blockIdx.z] + q) * 768 + head * HD;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float v[32];
+            tmem_ld32(row_tmem + (uint32_t)(32 * h), v);
+            if (q < T) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(dst + 32 * h + j) =
+                        make_float4(v[j] * inv, v[j + 1] * inv, v[j + 2] * inv, v[j + 3] * inv);
+            }
+        }
+    }
+    // every MMA this CTA issued has completed once its commits land; drain before freeing TMEM
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, ncols);
+    }
+}
+
+constexpr size_t att_smem(bool split) {
+    return (split ? AttCfg<true>::BYTES : AttCfg<false>::BYTES) + 1024;
+}
+
+}  // namespace
+
+cudaError_t attention_tc_init() {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)att_smem(true));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)att_smem(false));
+    return e;
+}
+
+cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st) {
+    const dim3 grid((s.max_len + QT - 1) / QT, 12, s.n);
+    if (split) attention_tc_kernel<true><<<grid, 128, att_smem(true), st>>>(qkv, s, ctx, err);
+    else attention_tc_kernel<false><<<grid, 128, att_smem(false), st>>>(qkv, s, ctx, err);
+    return cudaGetLastError();
+}
+
+}  // namespace rk

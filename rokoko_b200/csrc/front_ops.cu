@@ -3,7 +3,7 @@
 // every utterance of a batch at once (segmented row layout, front_ops.cuh).
 //
 // Reference semantics (src/kernels.cu): embeddings + LayerNorm :15-95,
-// residual LayerNorm :102-144, softmax :189-225, channel LayerNorm :364-404,
+// residual LayerNorm :102-144, channel LayerNorm :364-404,
 // AdaLayerNorm :513-548, sigmoid-sum :643-662, round/clamp durations
 // :1457-1479, alignment :1484-1505 (here a scan + index gather instead of a
 // dense 0/1 matrix and two GEMMs, src/rokoko.cpp:850-863, 916-919).
@@ -166,81 +166,6 @@ __global__ void adaln_concat_kernel(const float* __restrict__ x, RowMeta m, cons
     }
 }
 
-// Scaled dot-product attention without mask, FP32 (src/rokoko.cpp:363-384):
-// S = Q K^T * 0.125, softmax over keys, O = P V, within utterance blockIdx.z.
-// Block = 8 warps = 8 query rows of one head; keys / values staged through
-// shared memory in chunks.
-constexpr int ATT_ROWS = 8, ATT_CHUNK = 64, ATT_MAXT = 512;
-__global__ void attention_kernel(const float* __restrict__ qkv_all, SegMeta s, float* __restrict__ ctx_all) {
-    __shared__ float kv[ATT_CHUNK][65];
-    __shared__ float sc[ATT_ROWS][ATT_MAXT];
-    __shared__ float qs[ATT_ROWS][64];
-    const int T = s.len[blockIdx.z];
-    if ((int)blockIdx.x * ATT_ROWS >= T) return;  // uniform over the block
-    const float* qkv = qkv_all + (size_t)s.off[blockIdx.z] * 2304;
-    float* ctx = ctx_all + (size_t)s.off[blockIdx.z] * 768;
-    const int head = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * ATT_ROWS + w;
-    const bool row_ok = i < T;
-    if (row_ok) {
-        qs[w][lane] = qkv[(size_t)i * 2304 + head * 64 + lane];
-        qs[w][lane + 32] = qkv[(size_t)i * 2304 + head * 64 + lane + 32];
-    }
-    // scores
-    for (int j0 = 0; j0 < T; j0 += ATT_CHUNK) {
-        const int nj = min(ATT_CHUNK, T - j0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < nj * 64; e += blockDim.x) {
-            const int j = e >> 6, d = e & 63;
-            kv[j][d] = qkv[(size_t)(j0 + j) * 2304 + 768 + head * 64 + d];
-        }
-        __syncthreads();
-        if (row_ok)
-            for (int j = lane; j < nj; j += 32) {
-                float acc = 0.f;
-#pragma unroll 16
-                for (int d = 0; d < 64; d++) acc += qs[w][d] * kv[j][d];
-                sc[w][j0 + j] = acc * 0.125f;
-            }
-    }
-    // softmax over the row (max-subtracted exp, times 1/sum)
-    float inv = 0.f;
-    if (row_ok) {
-        float mx = -1e30f;
-        for (int j = lane; j < T; j += 32) mx = fmaxf(mx, sc[w][j]);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.f;
-        for (int j = lane; j < T; j += 32) {
-            const float e = expf(sc[w][j] - mx);
-            sc[w][j] = e;
-            sum += e;
-        }
-        inv = 1.0f / warp_sum(sum);
-    }
-    // O = P V
-    float o0 = 0.f, o1 = 0.f;
-    for (int j0 = 0; j0 < T; j0 += ATT_CHUNK) {
-        const int nj = min(ATT_CHUNK, T - j0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < nj * 64; e += blockDim.x) {
-            const int j = e >> 6, d = e & 63;
-            kv[j][d] = qkv[(size_t)(j0 + j) * 2304 + 1536 + head * 64 + d];
-        }
-        __syncthreads();
-        if (row_ok)
-            for (int j = 0; j < nj; j++) {
-                const float p = sc[w][j0 + j] * inv;
-                o0 += p * kv[j][lane];
-                o1 += p * kv[j][lane + 32];
-            }
-    }
-    if (row_ok) {
-        ctx[(size_t)i * 768 + head * 64 + lane] = o0;
-        ctx[(size_t)i * 768 + head * 64 + lane + 32] = o1;
-    }
-}
-
 // dur[r] = sum_50 sigmoid(proj[r]); int = max(1, round-half-even(dur)); gap rows 0
 __global__ void durations_kernel(const float* __restrict__ proj, RowMeta m, float* __restrict__ dur_f,
                                  int* __restrict__ dur_i) {
@@ -267,7 +192,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_gather_kernel(
     const int* __restrict__ dur, SegMeta tok, SegMeta frames, const float* __restrict__ cat,
     const float* __restrict__ te, float* __restrict__ en, float* __restrict__ asr, int* __restrict__ frame_tok,
     OpPlanes op, bool split) {
-    __shared__ int start[ATT_MAXT + 1];
+    __shared__ int start[512 + 1];
     __shared__ int warp_tot[ALIGN_THREADS / 32];
     const int u = blockIdx.y;
     const int T = tok.len[u], toff = tok.off[u];
@@ -357,9 +282,6 @@ void adaln_concat(const float* x, RowMeta m, const float* fc, int fc_stride, int
                   int style_stride, float* cat, OpPlanes op, bool split, cudaStream_t st) {
     adaln_concat_kernel<<<rows_grid(m.R), 256, 0, st>>>(x, m, fc, fc_stride, gamma_off, style, style_stride, cat, op,
                                                          split);
-}
-void attention(const float* qkv, SegMeta s, float* ctx, cudaStream_t st) {
-    attention_kernel<<<dim3((s.max_len + ATT_ROWS - 1) / ATT_ROWS, 12, s.n), 32 * ATT_ROWS, 0, st>>>(qkv, s, ctx);
 }
 void durations(const float* proj, RowMeta m, float* dur_f, int* dur_i, cudaStream_t st) {
     durations_kernel<<<rows_grid(m.R), 256, 0, st>>>(proj, m, dur_f, dur_i);

@@ -47,8 +47,11 @@ void ln_lrelu(const float* x, RowMeta m, const float* g, const float* b, float* 
 // gamma = fc + u*fc_stride + gamma_off, beta = gamma + 512, style = style + u*style_stride.
 void adaln_concat(const float* x, RowMeta m, const float* fc, int fc_stride, int gamma_off, const float* style,
                   int style_stride, float* cat, OpPlanes op, bool split, cudaStream_t st);
-// Scaled dot-product attention (12 heads of 64, no mask) within every segment.
-void attention(const float* qkv, SegMeta s, float* ctx, cudaStream_t st);
+// Scaled dot-product attention (12 heads of 64, no mask) within every segment,
+// on the tensor cores (attention_tc.cu): qkv [rows][2304] = [Q | K | V],
+// ctx [rows][768]; split = FP32 semantics (split-bf16 products), else fp16.
+cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st);
+cudaError_t attention_tc_init();
 void durations(const float* proj, RowMeta m, float* dur_f, int* dur_i, cudaStream_t st);
 // Duration -> alignment for every utterance: a block-wide scan of its durations
 // dur[tok.off .. +tok.len) gives token t's first frame; frame l < L of the

@@ -210,8 +210,12 @@ rk_status enqueue_token_phase(rk_ctx* c, RowMeta m, SegMeta seg, int B) {
     pack(r, f.h, 768, R, 768, f.op, F.qkv.Cp, sp);
     for (int layer = 0; layer < 12 && r.ok(); layer++) {
         linear(r, F.qkv, f.op, R, f.qkv);
-        attention(f.qkv, seg, f.ctx, r.st);
-        r.check_launch("attention");
+        {   // FP32 semantics in both precisions: the reference's FP16 build also keeps the
+            // attention GEMMs on FP32 data (src/rokoko_f16.cpp:227-244)
+            const cudaError_t e = attention_tc(f.qkv, seg, f.ctx, true, c->err, r.st);
+            r.check_launch("attention_tc");
+            if (e != cudaSuccess && r.ok()) r.status = fail_cuda_err(RK_ERR_LAUNCH, "attention_tc", e);
+        }
         pack(r, f.ctx, 768, R, 768, f.op, F.dense.Cp, sp);
         linear(r, F.dense, f.op, R, f.tmp);
         res_ln(f.h, f.tmp, m, F.attn_ln_w, F.attn_ln_b, planes(f.op, F.ffn.Cp), sp, r.st);

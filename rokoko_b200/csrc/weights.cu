@@ -511,6 +511,7 @@ rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
     if (upload_twiddles() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "twiddle upload");
     if (conv_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "conv kernel attributes");
     if (bilstm_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "lstm kernel attributes");
+    if (attention_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "attention kernel attributes");
     c->loaded = true;
     return RK_OK;
 }

@@ -69,3 +69,21 @@ def test_infer_fp32(gpu_ctx, oracle_model, n_phon, override):
     for n, r, t in report:
         assert r <= t, msg
     assert wav <= 1e-3, msg
+
+
+def test_albert_tensor_core_attention_t512(gpu_ctx, oracle_model):
+    """T = 512 (Kokoro's longest context, the shape of config 3): the ALBERT
+    stack with its attention on the tensor cores stays within 1e-4 of the FP32
+    oracle; durations are set to 1 frame per token so the decode is short."""
+    from rokoko_b200 import configs
+    u = configs.config3(seed=7)
+    assert u.tokens.shape[0] == 512
+    dov = np.ones(512, np.int32)
+    ref, ref_dur, ref_L, _ = oracle_model.infer(u.tokens, u.style, dov, bucket=32)
+    pcm, dur, L = gpu_ctx.infer(u.tokens, u.style, dov)
+    assert L == ref_L == 512 and np.array_equal(dur, ref_dur)
+    for name, tol in (("bert", 1e-4), ("d_en", 1e-4), ("text_enc", 1e-4), ("dur_enc", 1e-4)):
+        r = rel_l2(gpu_ctx.stage(name), oracle_model.stage(name))
+        print(f"T=512 {name}: {r:.3e}")
+        assert r <= tol, (name, r)
+    assert rel_l2(pcm, ref) <= 1e-3

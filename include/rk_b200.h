@@ -130,8 +130,22 @@ RK_API rk_status rk_conv1d_static_check(void* stream);
 /* ---- model context ------------------------------------------------------- */
 RK_API rk_status rk_create(int device, const rk_options* opts, rk_ctx** out);
 RK_API void rk_destroy(rk_ctx* ctx);
-/* KOKO v1 (fp32) or v2 (pre-baked fp16) bytes in host memory. */
+/* KOKO v1 (fp32), v2 (pre-baked fp16) or v3 (B200 layout, below) bytes in host memory. */
 RK_API rk_status rk_load_weights_koko(rk_ctx* ctx, const void* host_blob, size_t bytes);
+
+/* KOKO v3, the "B200 layout" file (the next step after the reference's v2
+ * converter, scripts/convert_v2.py:111-349, and its loader,
+ * src/weights.cpp:320-494): every weight already packed the way the kernels
+ * read it (K-major 16-bit planes, bf16 hi + lo for precision RK_PRECISION_FP32
+ * or fp16 for RK_PRECISION_FP16, weight norm folded in, output rows padded to
+ * the 128-row MMA tile, ConvTranspose1d split into its polyphase planes, LSTM
+ * biases summed, style FCs concatenated) in one image, so rk_load_weights_koko
+ * reads it with one device allocation and one copy.  Converts a v1 or v2 blob
+ * on the host (no GPU needed); *out_bytes receives the file size; dst NULL
+ * only sizes it.  A v3 file is read by a library build with the same weight
+ * layout and by a context of the same precision (else RK_ERR_WEIGHTS). */
+RK_API rk_status rk_convert_koko_b200(const void* host_blob, size_t bytes, int precision, void* dst, size_t cap,
+                                      size_t* out_bytes);
 
 /* Decoder + generator on given features, host buffers:
  * asr [L, 512], f0 [2L], n [2L], style [128] (acoustic half) -> pcm [600 L]. */

@@ -22,6 +22,7 @@ struct ConvW {
     void* hi = nullptr;                 // bf16 (split) or fp16
     void* lo = nullptr;                 // bf16 lo plane (split only)
     float* bias = nullptr;              // [C_out] or null
+    bool split = true;                  // planes are bf16 hi + lo (else one fp16 plane)
     CUtensorMap tm_hi{}, tm_lo{};
 };
 
@@ -205,6 +206,9 @@ struct rk_ctx {
     float* splitk[4] = {nullptr, nullptr, nullptr, nullptr};
     bool loaded = false;
     std::vector<void*> weight_allocs;
+    // the packed weights: one device allocation holding the whole weight image
+    void* weights_base = nullptr;
+    size_t weights_bytes = 0;
     rk::DecoderW dec;
     rk::FrontW front;
     bool has_front = false;

@@ -83,24 +83,190 @@ std::vector<float> KokoFile::f32(const std::string& name) const {
     return v;
 }
 
+// ------------------------------------------------------------------ weight image
+// Every device-resident weight byte is assembled in one host image (256-byte
+// aligned slices) while the structs are filled with tagged image offsets; the
+// image is uploaded with one allocation and one copy and the tagged pointers
+// are relocated.  The image together with the structs is also what a KOKO v3
+// ("B200 layout") file holds, so loading one is a copy plus tensor-map encoding.
+namespace {
+
+constexpr uint64_t kTag = 1ull << 62;  // never a device address; image offsets below 2^62
+
+bool tagged(const void* p) { return (reinterpret_cast<uint64_t>(p) & kTag) != 0; }
+
+}  // namespace
+
+void* Image::put(const void* h, size_t n) {
+    const size_t off = (bytes.size() + 255) & ~size_t(255);
+    bytes.resize(off + n, 0);
+    if (n) std::memcpy(bytes.data() + off, h, n);
+    return reinterpret_cast<void*>(kTag | off);
+}
+
+namespace {
+
+// Visitors over every device pointer and every packed conv of the weight structs.
+template <class F, class T>
+void vp(T*& p, F& f) {
+    void* v = p;
+    f(v);
+    p = static_cast<T*>(v);
+}
+template <class F> void visit(ConvW& w, F& f) { vp(w.hi, f); vp(w.lo, f); vp(w.bias, f); }
+template <class F> void visit(AdaINW& a, F& f) { vp(a.norm_w, f); vp(a.norm_b, f); }
+template <class F> void visit(StyleFC& s, F& f) { vp(s.w, f); vp(s.b, f); vp(s.out, f); }
+template <class F> void visit(ResBlk1dW& b, F& f) {
+    visit(b.conv1, f); visit(b.conv2, f); visit(b.conv1x1, f); visit(b.norm1, f); visit(b.norm2, f);
+    vp(b.pool_w, f); vp(b.pool_b, f);
+}
+template <class F> void visit(ResBlock1W& r, F& f) {
+    for (int j = 0; j < 3; j++) {
+        visit(r.convs1[j], f); visit(r.convs2[j], f); visit(r.adain1[j], f); visit(r.adain2[j], f);
+        vp(r.alpha1[j], f); vp(r.alpha2[j], f);
+    }
+}
+template <class F> void visit(LstmW& l, F& f) { visit(l.wih, f); vp(l.whh, f); }
+template <class F> void visit(DecoderW& d, F& f) {
+    vp(d.f0_conv_w, f); vp(d.f0_conv_b, f); vp(d.n_conv_w, f); vp(d.n_conv_b, f);
+    visit(d.asr_res, f); visit(d.encode, f);
+    for (auto& b : d.decode) visit(b, f);
+    for (auto& u : d.ups) visit(u, f);
+    for (auto& n : d.noise_convs) visit(n, f);
+    for (auto& n : d.noise_res) visit(n, f);
+    for (auto& r : d.resblocks) visit(r, f);
+    visit(d.conv_post, f); vp(d.source_w, f); vp(d.source_b, f); visit(d.fc, f);
+}
+template <class F> void visit(FrontW& F_, F& f) {
+    vp(F_.word, f); vp(F_.pos, f); vp(F_.type, f); vp(F_.emb_ln_w, f); vp(F_.emb_ln_b, f);
+    visit(F_.proj, f); visit(F_.qkv, f); visit(F_.dense, f); visit(F_.ffn, f); visit(F_.ffn_out, f);
+    visit(F_.bert_enc, f);
+    vp(F_.attn_ln_w, f); vp(F_.attn_ln_b, f); vp(F_.ffn_ln_w, f); vp(F_.ffn_ln_b, f); vp(F_.te_embed, f);
+    for (int i = 0; i < 3; i++) { visit(F_.te_conv[i], f); vp(F_.te_ln_g[i], f); vp(F_.te_ln_b[i], f); }
+    visit(F_.te_lstm, f);
+    for (auto& l : F_.dur_lstm) visit(l, f);
+    visit(F_.dur_final, f); visit(F_.shared, f); visit(F_.dur_proj, f);
+    for (int i = 0; i < 3; i++) { visit(F_.f0[i], f); visit(F_.nn[i], f); }
+    vp(F_.f0_proj_w, f); vp(F_.f0_proj_b, f); vp(F_.n_proj_w, f); vp(F_.n_proj_b, f);
+    visit(F_.fc, f);
+}
+
+// every packed conv of the structs (the ones with planes)
+template <class G> void each_conv(DecoderW& d, FrontW& F_, bool front, G&& g) {
+    std::vector<ConvW*> v;
+    auto rb1 = [&](ResBlk1dW& b) { v.push_back(&b.conv1); v.push_back(&b.conv2); v.push_back(&b.conv1x1); };
+    auto rb = [&](ResBlock1W& r) { for (int j = 0; j < 3; j++) { v.push_back(&r.convs1[j]); v.push_back(&r.convs2[j]); } };
+    v.push_back(&d.asr_res); rb1(d.encode);
+    for (auto& b : d.decode) rb1(b);
+    for (auto& u : d.ups) v.push_back(&u);
+    for (auto& n : d.noise_convs) v.push_back(&n);
+    for (auto& n : d.noise_res) rb(n);
+    for (auto& r : d.resblocks) rb(r);
+    v.push_back(&d.conv_post);
+    if (front) {
+        for (ConvW* w : {&F_.proj, &F_.qkv, &F_.dense, &F_.ffn, &F_.ffn_out, &F_.bert_enc, &F_.dur_proj}) v.push_back(w);
+        for (auto& c : F_.te_conv) v.push_back(&c);
+        v.push_back(&F_.te_lstm.wih);
+        for (auto& l : F_.dur_lstm) v.push_back(&l.wih);
+        v.push_back(&F_.dur_final.wih); v.push_back(&F_.shared.wih);
+        for (int i = 0; i < 3; i++) { rb1(F_.f0[i]); rb1(F_.nn[i]); }
+    }
+    for (ConvW* w : v)
+        if (w->hi) g(*w);
+}
+
+// One allocation + one copy of the image; tagged pointers -> device addresses; tensor maps.
+rk_status upload_image(rk_ctx* c, const Image& img, DecoderW& d, FrontW& F_, bool front) {
+    void* base = nullptr;
+    if (cudaMalloc(&base, std::max<size_t>(img.bytes.size(), 256)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(RK_ERR_OOM, "weight image allocation");
+    }
+    c->weight_allocs.push_back(base);
+    if (cudaMemcpy(base, img.bytes.data(), img.bytes.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, "weight image upload");
+    const uint64_t n = img.bytes.size();
+    bool bad = false;
+    auto reloc = [&](void*& p) {
+        if (!p) return;
+        const uint64_t v = reinterpret_cast<uint64_t>(p);
+        if (!(v & kTag) || (v & ~kTag) >= n) { bad = true; return; }
+        p = static_cast<char*>(base) + (v & ~kTag);
+    };
+    visit(d, reloc);
+    if (front) visit(F_, reloc);
+    if (bad) return fail(RK_ERR_WEIGHTS, "weight image: pointer outside the image");
+    bool maps_ok = true;
+    each_conv(d, F_, front, [&](ConvW& cw) {
+        const uint64_t cols = (uint64_t)cw.taps * cw.Cp;
+        const uint64_t rows = (uint64_t)conv_tc_weight_rows(cw.phases * cw.C_out);
+        maps_ok = maps_ok && make_tmap_k64(&cw.tm_hi, cw.hi, cw.split, cols, rows, cols, CONV_W_ROWS) &&
+                  (!cw.split || make_tmap_k64(&cw.tm_lo, cw.lo, true, cols, rows, cols, CONV_W_ROWS));
+        if (!cw.split) cw.tm_lo = cw.tm_hi;
+    });
+    if (!maps_ok) return fail(RK_ERR_INIT, "tensor map encoding failed (weights)");
+    c->weights_base = base;
+    c->weights_bytes = n;
+    return RK_OK;
+}
+
+// ------------------------------------------------------------------ KOKO v3 ("B200 layout")
+// [u32 magic KOKO][u32 version 3][u64 descriptor bytes]
+// descriptor: u32 precision | u32 has_front | u32 layout id | u32 0 | u64 sizeof(DecoderW) |
+//             u64 sizeof(FrontW) | u64 image bytes | DecoderW | FrontW (pointers as tagged image offsets)
+// zero pad to a multiple of 4096, then the image.  The structs are this build's in-memory
+// layout, so a v3 file is read only by a library with the same layout id.
+constexpr uint32_t kLayoutId = 0x52423301u ^ (uint32_t)(sizeof(ConvW) * 131 + sizeof(DecoderW) * 7 + sizeof(FrontW));
+
+struct V3Desc {
+    uint32_t precision, has_front, layout, zero;
+    uint64_t dec_bytes, front_bytes, image_bytes;
+};
+
+size_t v3_data_start(size_t desc_bytes) { return (16 + desc_bytes + 4095) / 4096 * 4096; }
+
+rk_status load_v3(rk_ctx* c, const uint8_t* blob, size_t n) {
+    uint64_t dlen = 0;
+    std::memcpy(&dlen, blob + 8, 8);
+    V3Desc h{};
+    if (dlen < sizeof(V3Desc) || 16 + dlen > n) return fail(RK_ERR_WEIGHTS, "KOKO v3: truncated descriptor");
+    std::memcpy(&h, blob + 16, sizeof h);
+    if (h.layout != kLayoutId || h.dec_bytes != sizeof(DecoderW) || h.front_bytes != sizeof(FrontW) ||
+        dlen != sizeof(V3Desc) + h.dec_bytes + h.front_bytes)
+        return fail(RK_ERR_WEIGHTS, "KOKO v3 file written by a library build with another weight layout; "
+                                    "re-export it from the v1 / v2 file");
+    if ((int)h.precision != c->precision)
+        return fail(RK_ERR_WEIGHTS, h.precision == RK_PRECISION_FP16
+                                        ? "KOKO v3 file holds FP16 planes; create the context with RK_PRECISION_FP16"
+                                        : "KOKO v3 file holds split-bf16 planes; create the context with RK_PRECISION_FP32");
+    const size_t start = v3_data_start(dlen);
+    if (start + h.image_bytes > n) return fail(RK_ERR_WEIGHTS, "KOKO v3: truncated image");
+    Image img;
+    img.bytes.assign(blob + start, blob + start + h.image_bytes);
+    std::memcpy(&c->dec, blob + 16 + sizeof(V3Desc), sizeof(DecoderW));
+    if (h.has_front) std::memcpy(&c->front, blob + 16 + sizeof(V3Desc) + sizeof(DecoderW), sizeof(FrontW));
+    c->has_front = h.has_front != 0;
+    return upload_image(c, img, c->dec, c->front, c->has_front);
+}
+
+}  // namespace
+
 // ------------------------------------------------------------------ loader
 namespace {
 
 float f16_round(float x) { return __half2float(__float2half_rn(x)); }
 
 struct Loader {
-    rk_ctx* c;
+    Image& img;
+    DecoderW& dec;
+    FrontW& front;
     const KokoFile& f;
     bool split;   // FP32 semantics (bf16 hi/lo planes)
     bool v2;      // file holds pre-baked FP16 weights
 
-    void* dev_upload(const void* h, size_t bytes) {
-        void* d = nullptr;
-        if (cudaMalloc(&d, bytes) != cudaSuccess) throw WeightError("cudaMalloc failed (weights)");
-        c->weight_allocs.push_back(d);
-        if (cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice) != cudaSuccess) throw WeightError("weight upload failed");
-        return d;
-    }
+    // every device-resident byte of the weights goes into one host image; the
+    // returned pointer is the image offset tagged (relocated after the upload)
+    void* dev_upload(const void* h, size_t bytes) { return img.put(h, bytes); }
     float* dev_f32(const std::vector<float>& v) { return static_cast<float*>(dev_upload(v.data(), v.size() * 4)); }
     float* dev_tensor(const std::string& name) { return dev_f32(f.f32(name)); }
 
@@ -160,15 +326,6 @@ struct Loader {
         throw WeightError("missing tensor " + vname + " (v2)");
     }
 
-    void make_maps(ConvW& cw) {
-        const uint64_t cols = (uint64_t)cw.taps * cw.Cp;
-        const uint64_t rows = (uint64_t)conv_tc_weight_rows(cw.phases * cw.C_out);
-        if (!make_tmap_k64(&cw.tm_hi, cw.hi, split, cols, rows, cols, CONV_W_ROWS) ||
-            (split && !make_tmap_k64(&cw.tm_lo, cw.lo, true, cols, rows, cols, CONV_W_ROWS)))
-            throw WeightError("tensor map encoding failed (weights)");
-        if (!split) cw.tm_lo = cw.tm_hi;
-    }
-
     // planes[row][col] <- host floats, converted to bf16 hi/lo or fp16.
     void upload_planes(ConvW& cw, const std::vector<float>& p_in) {
         // rows padded with zeros to a multiple of the kernel's 128-row weight tile
@@ -189,7 +346,7 @@ struct Loader {
             cw.hi = dev_upload(h.data(), n * 2);
             cw.lo = cw.hi;
         }
-        make_maps(cw);
+        cw.split = split;  // tensor maps are encoded after the upload (relocate_and_map)
     }
 
     // Conv1d (stride 1) from weight [Co][Ci][K] host floats.
@@ -275,10 +432,7 @@ struct Loader {
         fc.rows = fc_rows;
         fc.w = dev_f32(fcw);
         fc.b = dev_f32(fcb);
-        float* o = nullptr;
-        if (cudaMalloc(&o, (size_t)fc_rows * 4) != cudaSuccess) throw WeightError("cudaMalloc failed (fc)");
-        c->weight_allocs.push_back(o);
-        fc.out = o;
+        fc.out = dev_f32(std::vector<float>((size_t)fc_rows, 0.f));  // per-call output rows
         fcw.clear(); fcb.clear(); fc_rows = 0;
     }
 
@@ -340,7 +494,7 @@ struct Loader {
     }
 
     void load_decoder() {
-        DecoderW& d = c->dec;
+        DecoderW& d = dec;
         small_conv("decoder.F0_conv", &d.f0_conv_w, &d.f0_conv_b);
         small_conv("decoder.N_conv", &d.n_conv_w, &d.n_conv_b);
         // asr_res stays FP32 in the FP16 variant too (conv1d_f32 with FP32 weights,
@@ -412,7 +566,7 @@ struct Loader {
     }
 
     void load_front() {
-        FrontW& F = c->front;
+        FrontW& F = front;
         F.word = dev_tensor("bert.embeddings.word_embeddings.weight");
         F.pos = dev_tensor("bert.embeddings.position_embeddings.weight");
         F.type = dev_tensor("bert.embeddings.token_type_embeddings.weight");
@@ -473,6 +627,8 @@ struct Loader {
 void free_weights(rk_ctx* c) {
     for (void* p : c->weight_allocs) cudaFree(p);
     c->weight_allocs.clear();
+    c->weights_base = nullptr;
+    c->weights_bytes = 0;
     for (auto& p : c->splitk) p = nullptr;  // part of weight_allocs
     c->dec = DecoderW{};
     c->front = FrontW{};
@@ -480,24 +636,72 @@ void free_weights(rk_ctx* c) {
     c->loaded = false;
 }
 
-rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
+rk_status build_image(const void* blob, size_t bytes, int precision, Image& img, DecoderW& dec, FrontW& front,
+                      bool& has_front) {
     KokoFile f;
     std::string err;
     if (!f.parse(static_cast<const uint8_t*>(blob), bytes, err)) return fail(RK_ERR_WEIGHTS, err.c_str());
     const bool v2 = f.version == 2;
-    if (v2 && c->precision == RK_PRECISION_FP32)
+    if (v2 && precision == RK_PRECISION_FP32)
         return fail(RK_ERR_WEIGHTS, "KOKO v2 holds FP16 weights; create the context with RK_PRECISION_FP16");
-    free_weights(c);
     try {
-        Loader ld{c, f, c->precision == RK_PRECISION_FP32, v2};
+        Loader ld{img, dec, front, f, precision == RK_PRECISION_FP32, v2};
         ld.load_decoder();
         // the front half is optional: decoder-only files (and callers) use rk_decode_features
-        c->has_front = f.find("bert.embeddings.word_embeddings.weight") != nullptr;
-        if (c->has_front) ld.load_front();
+        has_front = f.find("bert.embeddings.word_embeddings.weight") != nullptr;
+        if (has_front) ld.load_front();
     } catch (WeightError& e) {
-        free_weights(c);
         return fail(RK_ERR_WEIGHTS, e.what());
     }
+    return RK_OK;
+}
+
+rk_status export_v3(int precision, const Image& img, const DecoderW& dec, const FrontW& front, bool has_front,
+                    void* dst, size_t cap, size_t* out_bytes) {
+    const size_t dlen = sizeof(V3Desc) + sizeof(DecoderW) + sizeof(FrontW);
+    const size_t start = v3_data_start(dlen), total = start + img.bytes.size();
+    if (out_bytes) *out_bytes = total;
+    if (!dst) return RK_OK;
+    if (cap < total) return fail(RK_ERR_WORKSPACE, "rk_export: destination smaller than the v3 file");
+    uint8_t* o = static_cast<uint8_t*>(dst);
+    std::memset(o, 0, start);
+    const uint32_t magic = 0x4F4B4F4Bu, version = 3;
+    const uint64_t dl = dlen;
+    std::memcpy(o, &magic, 4);
+    std::memcpy(o + 4, &version, 4);
+    std::memcpy(o + 8, &dl, 8);
+    const V3Desc h{(uint32_t)precision, has_front ? 1u : 0u, kLayoutId, 0u, sizeof(DecoderW), sizeof(FrontW),
+                   img.bytes.size()};
+    std::memcpy(o + 16, &h, sizeof h);
+    // the tensor maps are re-encoded when the file is loaded
+    DecoderW d = dec;
+    FrontW F_ = front;
+    auto clear_maps = [](ConvW& cw) { cw.tm_hi = CUtensorMap{}; cw.tm_lo = CUtensorMap{}; };
+    each_conv(d, F_, has_front, clear_maps);
+    std::memcpy(o + 16 + sizeof h, &d, sizeof d);
+    std::memcpy(o + 16 + sizeof h + sizeof d, &F_, sizeof F_);
+    std::memcpy(o + start, img.bytes.data(), img.bytes.size());
+    return RK_OK;
+}
+
+rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
+    const uint8_t* b = static_cast<const uint8_t*>(blob);
+    uint32_t magic = 0, version = 0;
+    if (bytes >= 16) { std::memcpy(&magic, b, 4); std::memcpy(&version, b + 4, 4); }
+    free_weights(c);
+    rk_status s;
+    if (magic == 0x4F4B4F4Bu && version == 3) {
+        s = load_v3(c, b, bytes);
+    } else {
+        Image img;
+        bool front = false;
+        s = build_image(blob, bytes, c->precision, img, c->dec, c->front, front);
+        if (!s) {
+            c->has_front = front;
+            s = upload_image(c, img, c->dec, c->front, c->has_front);
+        }
+    }
+    if (s) { free_weights(c); return s; }
     for (auto& p : c->splitk) {
         void* d = nullptr;
         if (cudaMalloc(&d, rk_ctx::kSplitKBytes) != cudaSuccess) {
@@ -517,3 +721,19 @@ rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes) {
 }
 
 }  // namespace rk
+
+// ------------------------------------------------------------------ C ABI: KOKO v3
+extern "C" rk_status rk_convert_koko_b200(const void* blob, size_t bytes, int precision, void* dst, size_t cap,
+                                          size_t* out_bytes) {
+    using namespace rk;
+    if (!blob) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_convert_koko_b200: null input");
+    if (precision != RK_PRECISION_FP32 && precision != RK_PRECISION_FP16)
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_convert_koko_b200: unknown precision");
+    Image img;
+    DecoderW dec;
+    FrontW front;
+    bool has_front = false;
+    rk_status s = build_image(blob, bytes, precision, img, dec, front, has_front);
+    if (s) return s;
+    return export_v3(precision, img, dec, front, has_front, dst, cap, out_bytes);
+}

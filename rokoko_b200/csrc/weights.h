@@ -32,6 +32,14 @@ struct KokoFile {
     std::vector<float> f32(const std::string& name) const;  // fp32 or fp16 -> float
 };
 
+// Host image of the packed weights: 256-byte aligned slices; put() returns the
+// slice's offset tagged as a pointer (relocated when the image is uploaded).
+struct Image {
+    std::vector<uint8_t> bytes;
+    void* put(const void* h, size_t n);
+};
+
+// KOKO v1 / v2 (packed on the host, uploaded as one image) or v3 (the image itself).
 rk_status load_weights(rk_ctx* c, const void* blob, size_t bytes);
 void free_weights(rk_ctx* c);
 

@@ -52,6 +52,9 @@ SIGNATURES = [
     ("rk_create", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(rk_options), ctypes.POINTER(ctypes.c_void_p)]),
     ("rk_destroy", None, [ctypes.c_void_p]),
     ("rk_load_weights_koko", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]),
+    ("rk_convert_koko_b200", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+      ctypes.POINTER(ctypes.c_size_t)]),
     ("rk_decode_features", ctypes.c_int, [ctypes.c_void_p, _f32p, _f32p, _f32p, _f32p, ctypes.c_int, _f32p]),
     ("rk_decode_features_device", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,

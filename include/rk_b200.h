@@ -173,6 +173,21 @@ RK_API rk_status rk_encode(rk_ctx* ctx, const int32_t* tokens, const int32_t* T_
                            const int32_t* dur_override, int32_t* dur_out, int32_t* L_out);
 RK_API rk_status rk_decode(rk_ctx* ctx, float* pcm_out, size_t pcm_capacity, size_t* n_samples, int* B_out);
 
+/* Streaming synthesis (TtsPipeline::synthesize_streaming, src/rokoko.h:298-360;
+ * the reference runs one chunk after the other): the B utterances (laid out as
+ * for rk_encode) are processed in chunks of `chunk`; while the decoder runs
+ * chunk k, the front half of chunk k + 1 runs beside it on the context's
+ * second stream.  on_pcm(user, index, pcm, n_samples) receives each
+ * utterance's PCM in order (pcm is a library buffer, valid during the call);
+ * it returns nonzero to go on and 0 to stop, after which rk_synthesize_stream
+ * returns RK_OK with nothing pending.  Durations are predicted unless
+ * dur_override (like tokens) is given.  No utterance of rk_encode may be
+ * pending. */
+typedef int (*rk_pcm_fn)(void* user, int index, const float* pcm, size_t n_samples);
+RK_API rk_status rk_synthesize_stream(rk_ctx* ctx, const int32_t* tokens, const int32_t* T_per_utt, int B,
+                                      const float* style, const int32_t* dur_override, int chunk,
+                                      rk_pcm_fn on_pcm, void* user);
+
 /* Stage activations of the last forward (names as the oracle's stage dumps);
  * copies min(count, cap) floats; *count = element count (0 if unknown). */
 RK_API rk_status rk_get_stage(rk_ctx* ctx, const char* name, float* host_dst, size_t cap, size_t* count);

@@ -168,6 +168,37 @@ class Context:
             off += ns[i]
         return out
 
+    def synthesize_stream(self, utterances, on_pcm, chunk: int = 8, overrides: bool = True) -> None:
+        """rk_synthesize_stream: the utterances (.tokens, .style, .durations as
+        overrides when `overrides`) in chunks of `chunk`, the front half of
+        chunk k + 1 overlapping the decode of chunk k.  on_pcm(index, pcm)
+        receives each utterance's PCM (a copy) in order and returns False to
+        stop."""
+        toks = [np.ascontiguousarray(u.tokens, np.int32).reshape(-1) for u in utterances]
+        Ts = np.array([t.shape[0] for t in toks], np.int32)
+        tok = np.ascontiguousarray(np.concatenate(toks), np.int32)
+        sty = np.ascontiguousarray(np.stack([np.asarray(u.style, np.float32).reshape(256) for u in utterances]))
+        dov = None
+        if overrides:
+            dov = np.ascontiguousarray(np.concatenate([np.asarray(u.durations, np.int32).reshape(-1)
+                                                       for u in utterances]), np.int32)
+        errors = []
+
+        def cb(_user, index, pcm, n):
+            try:
+                arr = np.ctypeslib.as_array(pcm, shape=(n,)).copy() if n else np.zeros(0, np.float32)
+                return 0 if on_pcm(index, arr) is False else 1
+            except BaseException as e:  # surfaced after the call
+                errors.append(e)
+                return 0
+
+        fn = lib.PCM_FN(cb)
+        lib.check(self._L.rk_synthesize_stream(self.h, _ip(tok), _ip(Ts), len(toks), _fp(sty),
+                                               _ip(dov) if dov is not None else None, int(chunk), fn, None),
+                  "rk_synthesize_stream")
+        if errors:
+            raise errors[0]
+
     def profile(self, on=True) -> None:
         """on: False / True (conv events) or a set of RK_PROFILE_* bits (CONV 1, SERIAL 2, TIMELINE 4)."""
         lib.check(self._L.rk_profile(self.h, int(on)), "rk_profile")

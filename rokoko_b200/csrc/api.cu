@@ -73,12 +73,14 @@ extern "C" rk_status rk_create(int device, const rk_options* opts, rk_ctx** out)
     }
     bool ok = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&c->enc, cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&c->rb[0], cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamCreateWithFlags(&c->rb[1], cudaStreamNonBlocking) == cudaSuccess;
     cudaEvent_t* evs[] = {&c->ev_fork, &c->ev_join, &c->ev_src[0], &c->ev_src[1], &c->ev_u, &c->ev_rb[0], &c->ev_rb[1],
                           &c->ev_sc[0], &c->ev_sc[1]};
     for (cudaEvent_t* e : evs) ok = ok && cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaMalloc(&c->err, 256) == cudaSuccess && cudaMemset(c->err, 0, 256) == cudaSuccess;
+    c->fst = c->stream;
     if (!ok) {
         rk_status s = fail_cuda(RK_ERR_CUDA, "rk_create");
         rk_destroy(c);
@@ -99,6 +101,8 @@ extern "C" void rk_destroy(rk_ctx* c) {
     free_weights(c);
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     for (cudaEvent_t e : c->tl_events) cudaEventDestroy(e);
+    for (cudaEvent_t e : {c->ev_chunk, c->ev_enc[0], c->ev_enc[1], c->ev_stage})
+        if (e) cudaEventDestroy(e);
     if (c->err) cudaFree(c->err);
     cudaEvent_t evs[] = {c->ev_fork, c->ev_join, c->ev_src[0], c->ev_src[1], c->ev_u, c->ev_rb[0], c->ev_rb[1],
                          c->ev_sc[0], c->ev_sc[1]};
@@ -106,6 +110,7 @@ extern "C" void rk_destroy(rk_ctx* c) {
         if (e) cudaEventDestroy(e);
     for (cudaStream_t s : c->rb)
         if (s) { cudaStreamSynchronize(s); cudaStreamDestroy(s); }
+    if (c->enc) { cudaStreamSynchronize(c->enc); cudaStreamDestroy(c->enc); }
     if (c->side) cudaStreamDestroy(c->side);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -318,7 +323,7 @@ rk_status decode_pending(rk_ctx* c, const rk_ctx::Pending& p, float* pcm, const 
 
 void drop_pending(rk_ctx* c, size_t keep) {
     c->pending.resize(std::min(keep, c->pending.size()));
-    if (c->pending.empty()) stash_reset(c);
+    if (c->pending.empty()) stash_reset(c, 0);
 }
 
 }  // namespace
@@ -387,4 +392,108 @@ extern "C" rk_status rk_decode(rk_ctx* c, float* pcm, size_t pcm_capacity, size_
     cudaStreamSynchronize(c->stream);
     drop_pending(c, 0);
     return s ? s : check_device_error(c);
+}
+
+// ------------------------------------------------------------------ streaming
+// rk_synthesize_stream: the utterances in chunks of `chunk`; chunk k's decodes
+// are enqueued on the decode streams, then chunk k + 1's front half runs on
+// the context's second stream (ctx->enc) while they execute, and the PCM of
+// chunk k is handed to the callback utterance by utterance once it is in host
+// memory.  Reference: TtsPipeline::synthesize_streaming (src/rokoko.h:298-360),
+// which runs its chunks one after the other.
+
+namespace {
+
+struct FrontStream {  // the front half on ctx->enc for the scope of a streaming call
+    rk_ctx* c;
+    explicit FrontStream(rk_ctx* c_) : c(c_) { c->fst = c->enc; }
+    ~FrontStream() { c->fst = c->stream; c->stash_pool = 0; }
+};
+
+rk_status ensure_pcm(rk_ctx* c, int i, size_t n) {
+    if (c->h_pcm_cap[i] >= n) return RK_OK;
+    if (c->h_pcm[i]) cudaFreeHost(c->h_pcm[i]);
+    c->h_pcm[i] = nullptr;
+    c->h_pcm_cap[i] = 0;
+    n = std::max(n, (size_t)1 << 20);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&c->h_pcm[i]), n * 4, cudaHostAllocPortable) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(RK_ERR_OOM, "rk_synthesize_stream: pinned PCM buffer");
+    }
+    c->h_pcm_cap[i] = n;
+    return RK_OK;
+}
+
+}  // namespace
+
+extern "C" rk_status rk_synthesize_stream(rk_ctx* c, const int32_t* tokens, const int32_t* T_per_utt, int B,
+                                          const float* style, const int32_t* dur_override, int chunk,
+                                          rk_pcm_fn on_pcm, void* user) {
+    if (!c || !tokens || !T_per_utt || !style || B < 1 || chunk < 1 || !on_pcm)
+        return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_synthesize_stream: bad argument");
+    if (!c->pending.empty())
+        return fail(RK_ERR_STATE, "rk_synthesize_stream: utterances from rk_encode are still pending (rk_decode first)");
+    DeviceGuard g(c->device);
+    for (cudaEvent_t* e : {&c->ev_chunk, &c->ev_enc[0], &c->ev_enc[1]})
+        if (!*e && cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess)
+            return fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event");
+    FrontStream fs(c);
+    const int n_chunks = (B + chunk - 1) / chunk;
+    std::vector<size_t> tok_off((size_t)B + 1, 0);
+    for (int b = 0; b < B; b++) {
+        if (T_per_utt[b] < 1) return fail(RK_ERR_CANNOT_IMPLEMENT, "rk_synthesize_stream: T out of range");
+        tok_off[b + 1] = tok_off[b] + (size_t)T_per_utt[b];
+    }
+    auto encode_chunk = [&](int k) {
+        const int b0 = k * chunk, nb = std::min(chunk, B - b0);
+        c->stash_pool = 1 + (k & 1);
+        stash_reset(c, c->stash_pool);  // chunk k - 2 of this pool has been decoded and handed out
+        rk_status s = encode_batch(c, tokens + tok_off[b0], T_per_utt + b0, nb, style + (size_t)b0 * 256,
+                                   dur_override ? dur_override + tok_off[b0] : nullptr, nullptr, nullptr,
+                                   "rk_synthesize_stream");
+        // encode_batch returns with the chunk's frame phase and F0 / N chains still queued on `enc`:
+        // its decodes (on the context stream) wait for them
+        if (!s && cudaEventRecord(c->ev_enc[k & 1], c->enc) != cudaSuccess)
+            s = fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event record");
+        return s;
+    };
+    auto abort_all = [&](rk_status s) {
+        cudaDeviceSynchronize();
+        c->pending.clear();
+        stash_reset(c, 1);
+        stash_reset(c, 2);
+        return s;
+    };
+    rk_status s = encode_chunk(0);
+    if (s) return abort_all(s);
+    for (int k = 0; k < n_chunks; k++) {
+        const int b0 = k * chunk, nb = std::min(chunk, B - b0);
+        // chunk k's entries are the first nb pending ones
+        size_t total = 0;
+        for (int i = 0; i < nb; i++) total += (size_t)600 * c->pending[i].L;
+        const int pb = k & 1;
+        if ((s = ensure_pcm(c, pb, total))) return abort_all(s);
+        if (cudaStreamWaitEvent(c->stream, c->ev_enc[k & 1], 0) != cudaSuccess)
+            return abort_all(fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event wait"));
+        std::vector<size_t> n_of(nb), at(nb);
+        size_t off = 0;
+        for (int i = 0; i < nb && !s; i++) {
+            at[i] = off;
+            n_of[i] = (size_t)600 * c->pending[i].L;
+            s = decode_pending(c, c->pending[i], c->h_pcm[pb] + off, "rk_synthesize_stream");
+            off += n_of[i];
+        }
+        if (s) return abort_all(s);
+        if (cudaEventRecord(c->ev_chunk, c->stream) != cudaSuccess)
+            return abort_all(fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event record"));
+        // the next chunk's front half overlaps this chunk's decode (its own stream, its own buffers)
+        if (k + 1 < n_chunks && (s = encode_chunk(k + 1))) return abort_all(s);
+        if (cudaEventSynchronize(c->ev_chunk) != cudaSuccess)
+            return abort_all(fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: decode"));
+        if ((s = check_device_error(c))) return abort_all(s);
+        c->pending.erase(c->pending.begin(), c->pending.begin() + nb);
+        for (int i = 0; i < nb; i++)
+            if (!on_pcm(user, b0 + i, c->h_pcm[pb] + at[i], n_of[i])) return abort_all(RK_OK);  // caller stopped
+    }
+    return RK_OK;
 }

@@ -276,8 +276,10 @@ __global__ void __launch_bounds__(320, 1)
                 // the reflection-pad duplicate row, if this pair holds it, takes the general path
                 const bool has_dup = args.dup_src_row >= orow_p && args.dup_src_row <= orow_last &&
                                      (args.dup_src_row - orow_p) % args.o_stride == 0;
+                const int pvalid = args.part_rows ? args.part_rows[mp >> 6] : 64;  // valid rows of this part
                 const bool fast = __all_sync(0xffffffffu, fast_conv && !has_dup && mp + 63 < args.M &&
-                                                              orow_p >= args.o_min && orow_last < args.T_out);
+                                                              orow_p >= args.o_min && orow_last < args.T_out &&
+                                                              pvalid == 64);
                 if (fast) {
                     // residual rows of both chunks in flight before the accumulator reads
                     const size_t rstep = (size_t)args.o_stride * args.ldres, ystep = (size_t)args.o_stride * args.ldy;
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(320, 1)
                     for (int j = 0; j < 64; j++) {
                         const int m = mp + j;
                         const int orow = orow_p + j * args.o_stride;
-                        if (m >= args.M || orow < args.o_min || orow >= args.T_out) continue;
+                        if (m >= args.M || orow < args.o_min || orow >= args.T_out || j >= pvalid) continue;
                         const float acc = tmem_ld1(s_tmem + (uint32_t)(2 * pp * 32 + j));
                         if (!co_ok) continue;
                         for (int pass = 0; pass < 2; pass++) {
@@ -401,6 +403,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const __grid_constan
         const int m = m0 + i;
         const int orow = m * a.o_stride + a.o_off + phase * a.o_phase_step;
         if (!co_ok || m >= a.M || orow < a.o_min || orow >= a.T_out) continue;
+        if (a.part_rows && (m & 63) >= a.part_rows[m >> 6]) continue;  // gap row between utterances
         for (int pass = 0; pass < 2; pass++) {
             int orw = orow, rrow = orow >> a.res_shift;
             if (pass == 1) {

@@ -49,6 +49,9 @@ struct ConvArgs {
     int stats_parts;      // ceil(M / 64) * phases
     int dup_src_row;      // >= 0: the accumulator of out_row == dup_src_row is also written to row 0
                           // (with residual row 0): reflection pad (1, 0) of the ConvTranspose output
+    const int* part_rows; // segmented rows (one phase only): rows [64p, 64p + part_rows[p]) of each 64-row
+                          //   part are valid; the others (gaps between utterances) are neither stored nor
+                          //   counted in the statistics; null = every row < M is valid
     uint32_t* err;        // device error word
     // filled by conv_tc_launch
     int k_split;          // > 1: the reduction is split over k_split CTAs per tile (see conv_tc_launch)

@@ -95,6 +95,7 @@ void conv(Run& r, const ConvCall& cc) {
     a.stats_ld = cc.stats_ld ? cc.stats_ld : w.C_out;
     a.stats_parts = stats_parts_for(cc);
     a.dup_src_row = cc.dup_src_row;
+    a.part_rows = cc.part_rows;
     a.err = r.c->err;
     rk_ctx* c = r.c;
     cudaEvent_t e1 = nullptr;
@@ -127,9 +128,13 @@ void conv(Run& r, const ConvCall& cc) {
 }
 
 void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, int Cp, bool split,
-          const float* coef, const float* snake, float slope, bool lrelu, int sr_stride, int sr_pad, int rows_dst) {
+          const float* coef, const float* snake, float slope, bool lrelu, int sr_stride, int sr_pad, int rows_dst,
+          SegRows sr, int coef_stride) {
     if (!r.ok()) return;
     PackArgs a{};
+    a.part_seg = sr.part_seg;
+    a.part_rows = sr.part_rows;
+    a.coef_stride = coef_stride;
     a.x = x; a.ldx = ldx; a.rows_src = rows; a.C = C;
     a.rows_dst = rows_dst >= 0 ? rows_dst : rows;
     a.Cp = Cp; a.hi = op.hi; a.lo = op.lo;
@@ -281,11 +286,10 @@ bool ev(cudaError_t e) { return e == cudaSuccess; }
 static size_t al(size_t x) { return (x + 255) & ~size_t(255); }
 
 void free_decode_ws(rk_ctx* c) {
+    // a decode may still be in flight (streaming calls grow the workspace while one runs)
+    if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second.exec);
     c->graphs.clear();
-    // the predictor graphs (F0 / N chains) also bake decode-workspace addresses
-    for (auto& kv : c->pgraphs) cudaGraphExecDestroy(kv.second.exec);
-    c->pgraphs.clear();
     for (void* p : c->ws.allocs) cudaFree(p);
     c->ws = DecodeWS{};
 }

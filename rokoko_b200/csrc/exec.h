@@ -6,6 +6,7 @@
 
 #include "../../include/rk_b200.h"
 #include "model.h"
+#include "ops.cuh"
 #include "status.h"
 
 namespace rk {
@@ -54,13 +55,14 @@ struct ConvCall {
     int act = 0;            // 1: GELU after bias
     bool use_bias = true;
     bool no_splitk = false; // never split the reduction (summation order independent of M)
+    const int* part_rows = nullptr;  // segmented rows: valid rows per 64-row part (ConvArgs::part_rows)
 };
 
 int stats_parts_for(const ConvCall& cc);
 void conv(Run& r, const ConvCall& cc);
 void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, int Cp, bool split,
           const float* coef = nullptr, const float* snake = nullptr, float slope = 0.f, bool lrelu = false,
-          int sr_stride = 1, int sr_pad = 0, int rows_dst = -1);
+          int sr_stride = 1, int sr_pad = 0, int rows_dst = -1, SegRows sr = SegRows{}, int coef_stride = 0);
 void coef(Run& r, const float* stats, int parts, int ld, int col0, const AdaINW& n, int T, const StyleFC& fc,
           Lane& ln);
 void record(Run& r, const char* name, const float* d, size_t n);

@@ -70,7 +70,7 @@ struct Req {
 // one cudaMalloc for a group of buffers (256-byte aligned slices); frees the group's previous allocation
 rk_status alloc_group(rk_ctx* c, std::vector<Req> reqs, std::vector<void*>& owner, const char* what) {
     if (!owner.empty()) {
-        cudaStreamSynchronize(c->stream);  // queued work may still use the old buffers
+        cudaDeviceSynchronize();  // queued work (either stream of the context) may still use the old buffers
         for (void* p : owner) cudaFree(p);
         owner.clear();
     }
@@ -136,29 +136,33 @@ rk_status ensure_frames(rk_ctx* c, int F) {
     return RK_OK;
 }
 
-rk_status ensure_pred(rk_ctx* c, int Lb) {
+// the batched F0 / N chains: R frame rows (x2 after the upsample), B utterances
+rk_status ensure_pred(rk_ctx* c, int R, int B) {
     FrontWS& f = c->fws;
-    if (f.cap_Lb >= Lb) return RK_OK;
-    // the predictor graphs bake these addresses
-    for (auto& kv : c->pgraphs) cudaGraphExecDestroy(kv.second.exec);
-    c->pgraphs.clear();
-    const size_t L = (size_t)Lb;
-    const size_t st = 2 * ((2 * L + STATS_ROWS - 1) / STATS_ROWS + 8) * 512 * 4;
+    if (f.cap_Rp >= R && f.cap_Bp >= B) return RK_OK;
+    R = std::max(R, f.cap_Rp);
+    B = std::max(B, f.cap_Bp);
+    const size_t r = (size_t)R;
+    const size_t st = 2 * (2 * r / 64 + 8) * 512 * 4;
+    const size_t plane = 2 * r * 512 * 2;
     std::vector<Req> reqs = {
-        {(void**)&f.shared, L * 512 * 4}, {(void**)&f.x1, L * 512 * 4}, {(void**)&f.x2, 2 * L * 256 * 4},
-        {(void**)&f.x3, 2 * L * 256 * 4}, {(void**)&f.stats, st}, {(void**)&f.stats2, st},
-        {(void**)&f.style1, 256 * 4}, {(void**)&f.f0, 2 * L * 4}, {(void**)&f.n, 2 * L * 4},
+        {(void**)&f.x1, r * 512 * 4}, {(void**)&f.x2, 2 * r * 256 * 4}, {(void**)&f.x3, 2 * r * 256 * 4},
+        {(void**)&f.r1, r * 512 * 4}, {(void**)&f.sc, r * 256 * 4}, {(void**)&f.coef, (size_t)B * 2 * 512 * 4},
+        {(void**)&f.stats, st}, {(void**)&f.stats2, st}, {(void**)&f.stats_a, st},
+        {(void**)&f.layout, (6 * r / 64 + 6 * (size_t)B) * 4}, {&f.op_p.hi, plane}, {&f.op_p.lo, plane},
     };
     rk_status s = alloc_group(c, reqs, f.pred_allocs, "front workspace allocation (predictor)");
-    if (s) { f.cap_Lb = 0; return s; }
-    f.cap_Lb = Lb;
+    if (s) { f.cap_Rp = f.cap_Bp = 0; return s; }
+    f.op_p.plane_bytes = plane;
+    f.cap_Rp = R;
+    f.cap_Bp = B;
     return RK_OK;
 }
 
 rk_status ensure_stage(rk_ctx* c, size_t bytes) {
     if (c->h_stage_bytes >= bytes) return RK_OK;
     if (c->h_stage) {
-        cudaStreamSynchronize(c->stream);
+        cudaDeviceSynchronize();  // no upload out of the old buffer may still be queued
         cudaFreeHost(c->h_stage);
         c->h_stage = nullptr;
         c->h_stage_bytes = 0;
@@ -176,7 +180,7 @@ rk_status ensure_stage(rk_ctx* c, size_t bytes) {
 float* stash_alloc(rk_ctx* c, size_t bytes) {
     bytes = al(bytes);
     for (auto& ch : c->stash)
-        if (ch.bytes - ch.used >= bytes) {
+        if (ch.pool == c->stash_pool && ch.bytes - ch.used >= bytes) {
             float* p = reinterpret_cast<float*>(ch.base + ch.used);
             ch.used += bytes;
             return p;
@@ -187,7 +191,7 @@ float* stash_alloc(rk_ctx* c, size_t bytes) {
         cudaGetLastError();
         return nullptr;
     }
-    c->stash.push_back({base, sz, bytes});
+    c->stash.push_back({base, sz, bytes, c->stash_pool});
     return reinterpret_cast<float*>(base);
 }
 
@@ -198,7 +202,7 @@ rk_status enqueue_token_phase(rk_ctx* c, RowMeta m, SegMeta seg, int B) {
     FrontW& F = c->front;
     FrontWS& f = c->fws;
     const bool sp = c->precision == RK_PRECISION_FP32;
-    Run r{c, c->stream, sp};
+    Run r{c, c->fst, sp};
     const int R = m.R;
     // prosody-style FCs of every utterance (AdaLayerNorm gamma / beta of the duration encoder)
     style_fc_batch(F.fc.w, F.fc.b, f.style + 128, 256, B, f.fc, F.fc.rows, r.st);
@@ -270,7 +274,7 @@ rk_status enqueue_frame_phase(rk_ctx* c, const int* dur_use, SegMeta tok, SegMet
     FrontW& Fw = c->front;
     FrontWS& f = c->fws;
     const bool sp = c->precision == RK_PRECISION_FP32;
-    Run r{c, c->stream, sp};
+    Run r{c, c->fst, sp};
     align_gather(dur_use, tok, frames, f.cat, f.te, f.en, asr_out, f.frame_tok, planes(f.op, 640), sp, r.st);
     r.check_launch("align_gather");
     lstm(r, Fw.shared, f.op, F, frames, f.shared_all);
@@ -278,66 +282,147 @@ rk_status enqueue_frame_phase(rk_ctx* c, const int* dur_use, SegMeta tok, SegMet
 }
 
 // ---------------------------------------------------------------- predictor
-// F0 / N chains of one utterance (src/rokoko.cpp:876-913) from fws.shared
-// [L_b][512] and the style in fws.style1 -> fws.f0 / fws.n [2 L_b].
-rk_status enqueue_predict_body(rk_ctx* c, int L_b) {
+// Frames of a batch in the segmented layout the F0 / N chains run on:
+// utterance u's L_b frames start at off[u], a multiple of 64, with at least one
+// zero-operand gap row after it (the K = 3 convs' padding), R rows in all.
+// After the x2 upsample of the chains every offset and length doubles.  Parts
+// (64 rows) never straddle two utterances, so the InstanceNorm partials the
+// conv epilogues write per part belong to one utterance each.
+struct FrameLayout {
+    int B = 0, R = 0;
+    std::vector<int> off, len;
+    // device: SegRows + AdaSegs of the base and the x2 layout
+    SegRows sr1, sr2;
+    AdaSegs as1, as2;
+};
+
+std::vector<int> frame_layout_host(const std::vector<int>& Lb, FrameLayout& L) {
+    const int B = (int)Lb.size();
+    L.B = B;
+    L.off.resize(B);
+    L.len = Lb;
+    int o = 0;
+    for (int b = 0; b < B; b++) {
+        L.off[b] = o;
+        o = (o + Lb[b] + 1 + 63) / 64 * 64;
+    }
+    L.R = (L.off[B - 1] + Lb[B - 1] + 63) / 64 * 64;
+    const int P = L.R / 64;
+    // [seg1 P | rows1 P | seg2 2P | rows2 2P | p0 B | np B | T B | p0_2 B | np_2 B | T_2 B]
+    std::vector<int> h((size_t)6 * P + 6 * B, 0);
+    int* seg1 = h.data();
+    int* rows1 = seg1 + P;
+    int* seg2 = rows1 + P;
+    int* rows2 = seg2 + 2 * P;
+    int* ab = rows2 + 2 * P;
+    for (int p = 0; p < P; p++) seg1[p] = -1;
+    for (int p = 0; p < 2 * P; p++) seg2[p] = -1;
+    for (int b = 0; b < B; b++) {
+        const int p0 = L.off[b] / 64, np = (Lb[b] + 63) / 64;
+        for (int p = p0; p < p0 + np; p++) {
+            seg1[p] = b;
+            rows1[p] = std::min(64, L.off[b] + Lb[b] - 64 * p);
+            const int v2 = 2 * rows1[p];
+            seg2[2 * p] = b;
+            rows2[2 * p] = std::min(64, v2);
+            if (v2 > 64) { seg2[2 * p + 1] = b; rows2[2 * p + 1] = v2 - 64; }
+        }
+        ab[b] = p0; ab[B + b] = np; ab[2 * B + b] = Lb[b];
+        ab[3 * B + b] = 2 * p0; ab[4 * B + b] = (2 * Lb[b] + 63) / 64; ab[5 * B + b] = 2 * Lb[b];
+    }
+    return h;
+}
+
+void frame_layout_device(const int* d, int g_stride, FrameLayout& L) {
+    const int P = L.R / 64, B = L.B;
+    L.sr1 = SegRows{d, d + P};
+    L.sr2 = SegRows{d + 2 * P, d + 4 * P};
+    const int* ab = d + 6 * P;
+    L.as1 = AdaSegs{ab, ab + B, ab + 2 * B, B, g_stride};
+    L.as2 = AdaSegs{ab + 3 * B, ab + 4 * B, ab + 5 * B, B, g_stride};
+}
+
+// AdainResBlk1d (src/rokoko.cpp:583-643) over the segmented rows of a batch:
+// per-utterance InstanceNorm statistics and AdaIN coefficients (gamma / beta
+// from each utterance's prosody style FC, fws.fc [B][rows]); x [R_in][ldx] with
+// partials stats_x over all parts of the input layout; y [R_out][ldy].
+void resblk1d_seg(Run& r, const ResBlk1dW& b, const FrameLayout& L, bool in_x2, const float* x, int ldx,
+                  const float* stats_x, float* y, int ldy, float* stats_y) {
+    FrontWS& f = r.c->fws;
+    const bool sp = r.split;
+    const bool out_x2 = in_x2 || b.upsample;
+    const int Rin = in_x2 ? 2 * L.R : L.R, Ro = out_x2 ? 2 * L.R : L.R;
+    const SegRows& sri = in_x2 ? L.sr2 : L.sr1;
+    const SegRows& sro = out_x2 ? L.sr2 : L.sr1;
+    const AdaSegs& asi = in_x2 ? L.as2 : L.as1;
+    const AdaSegs& aso = out_x2 ? L.as2 : L.as1;
+    const int parts_in = Rin / 64, parts_out = Ro / 64;
+    const float* res = x;
+    int ldres = ldx, shift = 0;
+    if (b.shortcut) {  // 1x1 conv at the input rows (the nearest upsample commutes with it)
+        pack(r, x, ldx, Rin, b.din, f.op_p, b.conv1x1.Cp, sp);
+        ConvCall cs;
+        cs.w = &b.conv1x1; cs.op = &f.op_p; cs.rows_in = Rin; cs.split = sp; cs.M = Rin; cs.T_out = Rin;
+        cs.y = f.sc; cs.ldy = b.dout; cs.use_bias = false; cs.no_splitk = true; cs.part_rows = sri.part_rows;
+        conv(r, cs);
+        res = f.sc; ldres = b.dout; shift = b.upsample ? 1 : 0;
+    }
+    auto coefs = [&](const float* stats, int parts, int ld, const AdaINW& n, const AdaSegs& as) {
+        if (!r.ok()) return;
+        adain_coef(stats, parts, ld, 0, n.C, 0, f.fc + n.fc_off, f.fc + n.fc_off + n.C, n.norm_w, n.norm_b, f.coef,
+                   r.st, as);
+        r.check_launch("adain_coef");
+    };
+    coefs(stats_x, parts_in, ldx, b.norm1, asi);
+    if (b.upsample) {
+        if (!r.ok()) return;
+        dw_upsample_pack(x, ldx, Rin, b.din, f.coef, f.coef + b.din, 0.2f, b.pool_w, b.pool_b, f.op_p.hi, f.op_p.lo,
+                         b.conv1.Cp, sp, r.st, sri, 2 * b.din);
+        r.check_launch("dw_upsample_pack");
+    } else {
+        pack(r, x, ldx, Rin, b.din, f.op_p, b.conv1.Cp, sp, f.coef, nullptr, 0.2f, true, 1, 0, -1, sri, 2 * b.din);
+    }
+    ConvCall c1;
+    c1.w = &b.conv1; c1.op = &f.op_p; c1.rows_in = Ro; c1.split = sp; c1.M = Ro; c1.T_out = Ro; c1.pad = 1;
+    c1.y = f.r1; c1.ldy = b.dout; c1.stats = f.stats_a; c1.stats_ld = b.dout; c1.no_splitk = true;
+    c1.part_rows = sro.part_rows;
+    conv(r, c1);
+    coefs(f.stats_a, parts_out, b.dout, b.norm2, aso);
+    pack(r, f.r1, b.dout, Ro, b.dout, f.op_p, b.conv2.Cp, sp, f.coef, nullptr, 0.2f, true, 1, 0, -1, sro,
+         2 * b.dout);
+    ConvCall c2;
+    c2.w = &b.conv2; c2.op = &f.op_p; c2.rows_in = Ro; c2.split = sp; c2.M = Ro; c2.T_out = Ro; c2.pad = 1;
+    c2.y = y; c2.ldy = ldy; c2.res = res; c2.ldres = ldres; c2.res_shift = shift;
+    c2.alpha = 1.0f / sqrtf(2.0f);
+    c2.stats = stats_y; c2.stats_ld = ldy; c2.no_splitk = true; c2.part_rows = sro.part_rows;
+    conv(r, c2);
+}
+
+// F0 / N chains of every utterance of the batch (src/rokoko.cpp:876-913) from
+// fws.shared_all (the shared LSTM's output in the segmented frame layout) ->
+// f0 / n [2R] in the x2 layout.
+rk_status enqueue_predict_batch(rk_ctx* c, const FrameLayout& L, float* f0, float* n) {
     FrontW& F = c->front;
     FrontWS& f = c->fws;
     const bool sp = c->precision == RK_PRECISION_FP32;
-    Run r{c, c->stream, sp};
-    style_fc(F.fc.w, F.fc.b, f.style1 + 128, F.fc.out, F.fc.rows, r.st);
-    r.check_launch("style_fc");
-    const int parts = conv_tc_stats_parts(L_b, 1);
-    col_stats(f.shared, 512, 0, 512, L_b, STATS_ROWS, f.stats, r.st);
-    r.check_launch("col_stats");
+    Run r{c, c->fst, sp};
     for (int chain = 0; chain < 2 && r.ok(); chain++) {
+        col_stats(f.shared_all, 512, 0, 512, L.R, STATS_ROWS, f.stats, r.st, L.sr1.part_rows);
+        r.check_launch("col_stats");
         const ResBlk1dW* b = chain == 0 ? F.f0 : F.nn;
-        resblk1d(r, b[0], f.shared, 512, f.stats, parts, 512, L_b, f.x1, 512, f.stats2, 512, F.fc);
-        resblk1d(r, b[1], f.x1, 512, f.stats2, parts, 512, L_b, f.x2, 256, f.stats, 256, F.fc);
-        resblk1d(r, b[2], f.x2, 256, f.stats, conv_tc_stats_parts(2 * L_b, 1), 256, 2 * L_b, f.x3, 256, nullptr, 0,
-                 F.fc);
-        rowdot(f.x3, 2 * L_b, 256, chain == 0 ? F.f0_proj_w : F.n_proj_w, chain == 0 ? F.f0_proj_b : F.n_proj_b,
-               chain == 0 ? f.f0 : f.n, r.st);
+        resblk1d_seg(r, b[0], L, false, f.shared_all, 512, f.stats, f.x1, 512, f.stats2);
+        resblk1d_seg(r, b[1], L, false, f.x1, 512, f.stats2, f.x2, 256, f.stats);
+        resblk1d_seg(r, b[2], L, true, f.x2, 256, f.stats, f.x3, 256, nullptr);
+        rowdot(f.x3, 2 * L.R, 256, chain == 0 ? F.f0_proj_w : F.n_proj_w, chain == 0 ? F.f0_proj_b : F.n_proj_b,
+               chain == 0 ? f0 : n, r.st);
         r.check_launch("rowdot");
-        if (chain == 0) {  // the N chain reuses the statistics buffer of `shared`
-            col_stats(f.shared, 512, 0, 512, L_b, STATS_ROWS, f.stats, r.st);
-            r.check_launch("col_stats");
-        }
     }
     return r.status;
-}
-
-rk_status enqueue_predict(rk_ctx* c, int L_b) {
-    if (c->record || !c->use_graphs) return enqueue_predict_body(c, L_b);
-    auto it = c->pgraphs.find(L_b);
-    if (it == c->pgraphs.end()) {
-        const long long before = c->launches;
-        if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, "predictor graph capture begin");
-        rk_status s = enqueue_predict_body(c, L_b);
-        cudaGraph_t g = nullptr;
-        cudaError_t e = cudaStreamEndCapture(c->stream, &g);
-        if (s != RK_OK) { if (g) cudaGraphDestroy(g); cudaGetLastError(); return s; }
-        if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "predictor graph capture end", e);
-        rk_ctx::GraphRec rec;
-        e = cudaGraphInstantiateWithFlags(&rec.exec, g, 0);
-        cudaGraphDestroy(g);
-        if (e != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "predictor graph instantiate", e);
-        rec.launches = c->launches - before;
-        c->launches = before;
-        it = c->pgraphs.emplace(L_b, std::move(rec)).first;
-    }
-    cudaError_t e = cudaGraphLaunch(it->second.exec, c->stream);
-    if (e != cudaSuccess) return fail_cuda_err(RK_ERR_LAUNCH, "predictor graph launch", e);
-    c->launches += it->second.launches;
-    return RK_OK;
 }
 
 }  // namespace
 
 void free_front_ws(rk_ctx* c) {
-    for (auto& kv : c->pgraphs) cudaGraphExecDestroy(kv.second.exec);
-    c->pgraphs.clear();
     FrontWS& f = c->fws;
     for (void* p : f.row_allocs) cudaFree(p);
     for (void* p : f.frame_allocs) cudaFree(p);
@@ -349,15 +434,16 @@ void free_front_ws(rk_ctx* c) {
     if (c->h_stage) cudaFreeHost(c->h_stage);
     c->h_stage = nullptr;
     c->h_stage_bytes = 0;
+    for (int i = 0; i < 2; i++) {
+        if (c->h_pcm[i]) cudaFreeHost(c->h_pcm[i]);
+        c->h_pcm[i] = nullptr;
+        c->h_pcm_cap[i] = 0;
+    }
 }
 
-void destroy_predict_graphs(rk_ctx* c) {
-    for (auto& kv : c->pgraphs) cudaGraphExecDestroy(kv.second.exec);
-    c->pgraphs.clear();
-}
-
-void stash_reset(rk_ctx* c) {
-    for (auto& ch : c->stash) ch.used = 0;
+void stash_reset(rk_ctx* c, int pool) {
+    for (auto& ch : c->stash)
+        if (ch.pool == pool) ch.used = 0;
 }
 
 rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, int B, const float* style,
@@ -393,6 +479,9 @@ rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, i
     if (!s) s = ensure_stage(c, std::max(n_meta * 4 + (size_t)B * 256 * 4, (size_t)R * 4 * 2 + 4 * (size_t)B * 4));
     if (s) return s;
     FrontWS& f = c->fws;
+    // the previous batch's last uploads out of the staging buffer must be done before it is rewritten
+    if (c->ev_stage && cudaEventSynchronize(c->ev_stage) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, (w + ": staging buffer").c_str());
     int* hm = static_cast<int*>(c->h_stage);
     int* h_tok = hm;
     int* h_pos = hm + R;
@@ -416,7 +505,7 @@ rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, i
     std::memcpy(hm + 3 * R + B, len.data(), (size_t)B * 4);
     float* h_style = reinterpret_cast<float*>(hm + n_meta);
     std::memcpy(h_style, style, (size_t)B * 256 * 4);
-    cudaStream_t st = c->stream;
+    cudaStream_t st = c->fst;
     if (c->record) c->stages.clear();
     f.len0 = len[0];
     if (cudaMemcpyAsync(f.meta, hm, n_meta * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -432,49 +521,61 @@ rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, i
         cudaStreamSynchronize(st) != cudaSuccess)
         return fail_cuda(RK_ERR_CUDA, (w + ": duration read-back").c_str());
     const int bucket = c->l_bucket > 1 ? c->l_bucket : 1;
-    std::vector<int> L(B), Lb(B), foff(B);
-    int* h_use = hm + R;  // dur_use in the segmented layout
-    int F = 0, Lbmax = 0;
+    std::vector<int> L(B), Lb(B);
+    std::vector<int> use((size_t)R, 0);  // durations used (override or predicted), segmented layout
+    int Lbmax = 0;
     {
         size_t k = 0;
         for (int b = 0; b < B; b++) {
             long long sum = 0;
             for (int t = 0; t < len[b]; t++, k++) {
                 const int pred = h_dur[off[b] + t];
-                const int use = dur_override ? dur_override[k] : pred;
+                const int u = dur_override ? dur_override[k] : pred;
                 if (dur_out) dur_out[k] = pred;
-                h_use[off[b] + t] = use;
-                sum += use;
+                use[off[b] + t] = u;
+                sum += u;
             }
-            for (int g = 0; g < SEG_GAP; g++) h_use[off[b] + len[b] + g] = 0;
             if (sum < 1 || sum > 64 * 1024) return bad("total duration out of range");
             L[b] = (int)sum;
             Lb[b] = (int)((sum + bucket - 1) / bucket * bucket);  // src/rokoko.cpp:797-802
-            foff[b] = F;
-            F += Lb[b];
             Lbmax = std::max(Lbmax, Lb[b]);
             if (L_out) L_out[b] = L[b];
         }
     }
+    // segmented frame layout of the batch (64-aligned utterances, gap rows between)
+    FrameLayout lay;
+    const std::vector<int> tables = frame_layout_host(Lb, lay);
+    const int F = lay.R;
     s = ensure_frames(c, F);
     if (!s) s = ensure_ig_op(c, (size_t)F, (size_t)F * 640 * 2);
-    if (!s) s = ensure_pred(c, Lbmax);
+    if (!s) s = ensure_pred(c, F, B);
     if (!s) s = ensure_decode_ws(c, Lbmax);
+    if (!s) s = ensure_stage(c, (size_t)R * 4 * 2 + 2 * (size_t)B * 4 + tables.size() * 4);
     if (s) return s;
+    hm = static_cast<int*>(c->h_stage);  // may have moved in ensure_stage: the durations were consumed
     // stash of the batch's decoder inputs: asr [F][512], f0 / n [2F], style [B][128]
     float* st_asr = stash_alloc(c, (size_t)F * 512 * 4);
     float* st_f0 = st_asr ? stash_alloc(c, (size_t)2 * F * 4) : nullptr;
     float* st_n = st_f0 ? stash_alloc(c, (size_t)2 * F * 4) : nullptr;
     float* st_style = st_n ? stash_alloc(c, (size_t)B * 128 * 4) : nullptr;
     if (!st_style) return fail(RK_ERR_OOM, (w + ": pending-utterance stash").c_str());
-    int* h_foff = hm + 2 * R;
-    std::memcpy(h_foff, foff.data(), (size_t)B * 4);
-    std::memcpy(h_foff + B, Lb.data(), (size_t)B * 4);
+    int* h_use = hm + R;
+    std::memcpy(h_use, use.data(), (size_t)R * 4);
+    int* h_fseg = hm + 2 * R;
+    std::memcpy(h_fseg, lay.off.data(), (size_t)B * 4);
+    std::memcpy(h_fseg + B, Lb.data(), (size_t)B * 4);
+    int* h_tab = h_fseg + 2 * B;
+    std::memcpy(h_tab, tables.data(), tables.size() * 4);
     // dur_use goes where tok[] was (the token phase is done with it), frame segments after utt[]
     int* d_fseg = f.meta + 2 * R;
     if (cudaMemcpyAsync(f.meta, h_use, (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(d_fseg, h_foff, (size_t)2 * B * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        cudaMemcpyAsync(d_fseg, h_fseg, (size_t)2 * B * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(f.layout, h_tab, tables.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
         return fail_cuda(RK_ERR_CUDA, (w + ": duration upload").c_str());
+    if ((!c->ev_stage && cudaEventCreateWithFlags(&c->ev_stage, cudaEventDisableTiming) != cudaSuccess) ||
+        cudaEventRecord(c->ev_stage, st) != cudaSuccess)
+        return fail_cuda(RK_ERR_CUDA, (w + ": staging event").c_str());
+    frame_layout_device(f.layout, c->front.fc.rows, lay);
     SegMeta frames{d_fseg, d_fseg + B, B, Lbmax};
     s = enqueue_frame_phase(c, f.meta, seg, frames, F, st_asr);
     if (s) { cudaStreamSynchronize(st); return s; }
@@ -492,29 +593,19 @@ rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, i
         record(r, "asr_aligned", st_asr, (size_t)Lb[0] * 512);
         if (r.status) return r.status;
     }
-    // ---- per utterance: F0 / N chains, results into the stash
-    for (int b = 0; b < B; b++) {
-        if (cudaMemcpyAsync(f.shared, f.shared_all + (size_t)foff[b] * 512, (size_t)Lb[b] * 512 * 4,
-                            cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-            cudaMemcpyAsync(f.style1, f.style + (size_t)b * 256, 256 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, (w + ": predictor inputs").c_str());
-        s = enqueue_predict(c, Lb[b]);
-        if (s) { cudaStreamSynchronize(st); return s; }
-        if (c->record && b == 0) {
-            Run r{c, st, c->precision == RK_PRECISION_FP32};
-            record(r, "f0_pred", f.f0, (size_t)2 * Lb[0]);
-            record(r, "n_pred", f.n, (size_t)2 * Lb[0]);
-            if (r.status) return r.status;
-        }
-        if (cudaMemcpyAsync(st_f0 + (size_t)2 * foff[b], f.f0, (size_t)2 * Lb[b] * 4, cudaMemcpyDeviceToDevice, st) !=
-                cudaSuccess ||
-            cudaMemcpyAsync(st_n + (size_t)2 * foff[b], f.n, (size_t)2 * Lb[b] * 4, cudaMemcpyDeviceToDevice, st) !=
-                cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, (w + ": predictor outputs").c_str());
+    // ---- F0 / N chains of the whole batch, straight into the stash (x2 layout)
+    s = enqueue_predict_batch(c, lay, st_f0, st_n);
+    if (s) { cudaStreamSynchronize(st); return s; }
+    {
+        Run r{c, st, c->precision == RK_PRECISION_FP32};
+        record(r, "f0_pred", st_f0, (size_t)2 * Lb[0]);
+        record(r, "n_pred", st_n, (size_t)2 * Lb[0]);
+        if (r.status) return r.status;
     }
     if (cudaMemcpy2DAsync(st_style, 128 * 4, f.style, 256 * 4, 128 * 4, B, cudaMemcpyDeviceToDevice, st) !=
         cudaSuccess)
         return fail_cuda(RK_ERR_CUDA, (w + ": style stash").c_str());
+    std::vector<int> foff = lay.off;
     for (int b = 0; b < B; b++)
         c->pending.push_back({L[b], Lb[b], st_asr + (size_t)foff[b] * 512, st_f0 + (size_t)2 * foff[b],
                               st_n + (size_t)2 * foff[b], st_style + (size_t)b * 128});

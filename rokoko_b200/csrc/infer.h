@@ -12,7 +12,7 @@ namespace rk {
 // context's stash.  Synchronous with respect to the duration read-back only.
 rk_status encode_batch(rk_ctx* c, const int32_t* tokens, const int32_t* T_per, int B, const float* style,
                        const int32_t* dur_override, int32_t* dur_out, int32_t* L_out, const char* who);
-// Marks every stash chunk free again (call when no utterance is pending).
-void stash_reset(rk_ctx* c);
+// Marks the stash chunks of `pool` free again (call when none of its utterances is pending).
+void stash_reset(rk_ctx* c, int pool = 0);
 void free_front_ws(rk_ctx* c);
 }  // namespace rk

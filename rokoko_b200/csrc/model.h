@@ -144,11 +144,12 @@ struct DecodeWS {
 // Front-half workspace.  Three groups, each grown on demand:
 //   rows    token rows of a batch in the segmented layout (front_ops.cuh):
 //           cap_R rows, cap_B utterances;
-//   frames  decoder frames of a batch (utterance b's L_b frames at frame_off[b]):
-//           cap_F rows, plus the LSTM input-gate and operand buffers sized for
-//           both row and frame phases;
-//   pred    one utterance's predictor (F0 / N chains) of up to cap_Lb frames;
-//           the predictor graphs bake these addresses.
+//   frames  decoder frames of a batch in the segmented frame layout (utterance
+//           b's L_b frames at a 64-aligned offset, gap rows between): cap_F
+//           rows, plus the LSTM input-gate and operand buffers sized for both
+//           row and frame phases;
+//   pred    the batch's F0 / N chains over the same frames (and their x2
+//           upsampled layout).
 struct FrontWS {
     int cap_R = 0, cap_B = 0;
     std::vector<void*> row_allocs;
@@ -166,10 +167,13 @@ struct FrontWS {
     float* ig = nullptr;            // [rows][2048] LSTM input gates
     Operand op;
     int len0 = 0;                   // token count of the batch's first utterance (stage capture)
-    int cap_Lb = 0;
+    // the batched F0 / N chains over the segmented frame rows (capacity cap_Rp rows, cap_Bp utterances)
+    int cap_Rp = 0, cap_Bp = 0;
     std::vector<void*> pred_allocs;
-    float *shared = nullptr, *x1 = nullptr, *x2 = nullptr, *x3 = nullptr, *stats = nullptr, *stats2 = nullptr,
-          *style1 = nullptr, *f0 = nullptr, *n = nullptr;
+    float *x1 = nullptr, *x2 = nullptr, *x3 = nullptr, *r1 = nullptr, *sc = nullptr, *coef = nullptr,
+          *stats = nullptr, *stats2 = nullptr, *stats_a = nullptr;
+    int* layout = nullptr;  // segment tables of the frame layout (device)
+    Operand op_p;
 };
 
 struct StageRec {  // captured stage activations (rk_record_stages)
@@ -191,6 +195,8 @@ struct rk_ctx {
     int max_tokens = 512;
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // SineGen / STFT / noise branch
+    cudaStream_t enc = nullptr;   // front half while a streaming call decodes the previous chunk
+    cudaStream_t fst = nullptr;   // the stream the front half is enqueued on (stream or enc)
     cudaStream_t rb[2] = {nullptr, nullptr};  // resblock lanes 1 and 2
     // fork/join events: fork (main -> side), src[i] (side -> main, noise branch i
     // done), u (main -> resblock lanes), rb[j] (resblock lane j -> main)
@@ -240,8 +246,6 @@ struct rk_ctx {
     std::vector<double> prof_flops;        // algorithmic FLOPs of each timed launch
     double prof_ms_acc = 0.0, prof_flops_acc = 0.0;
     long long prof_launches_acc = 0;
-    // predictor graphs (one utterance's F0 / N chains) keyed by L_b
-    std::map<int, GraphRec> pgraphs;
     // utterances encoded by rk_encode and not yet decoded: their decoder inputs
     // (asr [L_b][512], f0 / n [2 L_b], style [128]) live in the stash chunks
     struct Pending {
@@ -252,9 +256,17 @@ struct rk_ctx {
     struct StashChunk {
         char* base;
         size_t bytes, used;
+        int pool;  // 0: rk_encode / rk_infer; 1, 2: alternate chunks of a streaming call
     };
     std::vector<StashChunk> stash;
+    int stash_pool = 0;  // pool the next encode allocates from
+    // pinned PCM of the chunks of a streaming call (double-buffered)
+    float* h_pcm[2] = {nullptr, nullptr};
+    size_t h_pcm_cap[2] = {0, 0};
+    cudaEvent_t ev_chunk = nullptr;
+    cudaEvent_t ev_enc[2] = {nullptr, nullptr};  // a streaming chunk's front half is done (on `enc`)
     // pinned host staging for the batch metadata upload and the duration read-back
     void* h_stage = nullptr;
     size_t h_stage_bytes = 0;
+    cudaEvent_t ev_stage = nullptr;  // the last uploads out of h_stage are done
 };

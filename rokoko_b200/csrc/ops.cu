@@ -60,29 +60,44 @@ __global__ void style_fc_kernel(const float* __restrict__ W, const float* __rest
 // slices.  mean = S / T, var = Q / T - mean^2 (biased, the reference's
 // single-pass form), scale = (1 + gamma) w / sqrt(var + 1e-5),
 // shift = (1 + gamma)(b - w mean / sqrt(var + eps)) + beta.
+// Segmented form (seg != null): blockIdx.y = segment u, which owns parts
+// [seg.p0[u], seg.p0[u] + seg.np[u]) of rows seg.T[u]; its gamma / beta are
+// offset by u * seg.g_stride and its coefficients by u * 2C; the squares of the
+// statistics sit `parts` (all parts of the array) after the sums.
 __global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restrict__ stats, int parts, int ld,
                                                           int col0, int C, int T, const float* __restrict__ gamma,
                                                           const float* __restrict__ beta,
                                                           const float* __restrict__ nw,
-                                                          const float* __restrict__ nb, float* __restrict__ coef) {
+                                                          const float* __restrict__ nb, float* __restrict__ coef,
+                                                          AdaSegs seg) {
     __shared__ double sh_s[128][8], sh_q[128][8];
     const int cx = threadIdx.x, py = threadIdx.y;
     const int c = blockIdx.x * 8 + cx;
+    int pbase = 0, np = parts;
+    if (seg.p0) {
+        const int u = blockIdx.y;
+        pbase = seg.p0[u];
+        np = seg.np[u];
+        T = seg.T[u];
+        gamma += (size_t)u * seg.g_stride;
+        beta += (size_t)u * seg.g_stride;
+        coef += (size_t)u * 2 * C;
+    }
     double s = 0.0, q = 0.0;
-    if (c < C) {
+    if (c < C && np > 0) {
         // eight parts per slice in flight at once: addresses clamped to the last
         // part, the sums predicated (parts ascending, as a serial loop would add them)
-        for (int p0 = py; p0 < parts; p0 += 8 * 128) {
+        for (int p0 = py; p0 < np; p0 += 8 * 128) {
             float sv[8], qv[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                const int pc = min(p0 + u * 128, parts - 1);
+                const int pc = pbase + min(p0 + u * 128, np - 1);
                 sv[u] = stats[(size_t)pc * ld + col0 + c];
                 qv[u] = stats[(size_t)(parts + pc) * ld + col0 + c];
             }
 #pragma unroll
             for (int u = 0; u < 8; u++)
-                if (p0 + u * 128 < parts) {
+                if (p0 + u * 128 < np) {
                     s += sv[u];
                     q += qv[u];
                 }
@@ -98,7 +113,7 @@ __global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restric
         }
         __syncthreads();
     }
-    if (py != 0 || c >= C) return;
+    if (py != 0 || c >= C || T < 1) return;
     const double mean_d = sh_s[0][cx] / T;
     const double var_d = sh_q[0][cx] / T - mean_d * mean_d;
     const float mean = (float)mean_d;
@@ -114,12 +129,13 @@ __global__ void __launch_bounds__(1024) adain_coef_kernel(const float* __restric
 // slice sums in order.
 __global__ void __launch_bounds__(256) col_stats_kernel(const float* __restrict__ x, int ld, int col0, int ncols,
                                                         int T, int rows_per_part, int parts,
-                                                        float* __restrict__ stats) {
+                                                        float* __restrict__ stats, const int* __restrict__ part_rows) {
     __shared__ float sh_s[8][32], sh_q[8][32];
     const int cx = threadIdx.x, sy = threadIdx.y;
     const int c = blockIdx.x * 32 + cx;
     const int p = blockIdx.y;
-    const int r0 = p * rows_per_part, r1 = min(T, r0 + rows_per_part);
+    const int r0 = p * rows_per_part;
+    const int r1 = part_rows ? r0 + part_rows[p] : min(T, r0 + rows_per_part);
     float s = 0.f, q = 0.f;
     if (c < ncols) {
 #pragma unroll 4
@@ -176,22 +192,34 @@ __global__ void concat_cols_kernel(float* dst, int ld, int col0, int T, const fl
     }
 }
 
+// Segmented form (sr.part_seg != null): the input rows are a segmented layout
+// (SegRows); an output row belongs to its input row's segment, gap rows are
+// written as zeros, inputs outside the row's segment count as zeros (the
+// utterance's own boundary), and the AdaIN coefficients of segment u sit at
+// scale + u * cstride.
+__device__ __forceinline__ int seg_of_row(const SegRows& sr, int r) {
+    const int p = r >> 6;
+    return (r & 63) < sr.part_rows[p] ? sr.part_seg[p] : -1;
+}
+
 template <bool SPLIT, typename I>
 __global__ void dw_upsample_pack_kernel(const float* __restrict__ x, int ldx, int T, int C,
                                         const float* __restrict__ scale, const float* __restrict__ shift,
                                         float slope, const float* __restrict__ w, const float* __restrict__ bias,
-                                        void* hi, void* lo, int Cp) {
+                                        void* hi, void* lo, int Cp, SegRows sr, int cstride) {
     const int To = 2 * T;
     const I total = (I)To * Cp;
     for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
         const int t = (int)(i / Cp), c = (int)(i - (I)t * Cp);
         float v = 0.f;
-        if (c < C) {
+        const int u = sr.part_seg ? seg_of_row(sr, t >> 1) : 0;
+        if (c < C && u >= 0) {
+            const float sc = scale[(size_t)u * cstride + c], sh = shift[(size_t)u * cstride + c];
             float acc = 0.f;
             for (int k = 0; k < 3; k++) {
                 const int tu = t + 1 - k;
-                if (tu >= 0 && (tu & 1) == 0 && (tu >> 1) < T) {
-                    float a = scale[c] * x[(size_t)(tu >> 1) * ldx + c] + shift[c];
+                if (tu >= 0 && (tu & 1) == 0 && (tu >> 1) < T && (!sr.part_seg || seg_of_row(sr, tu >> 1) == u)) {
+                    float a = sc * x[(size_t)(tu >> 1) * ldx + c] + sh;
                     a = a > 0.f ? a : slope * a;
                     acc += w[c * 3 + k] * a;
                 }
@@ -376,16 +404,16 @@ void style_fc_batch(const float* W, const float* b, const float* s, int s_stride
 }
 
 void adain_coef(const float* stats, int parts, int ld, int col0, int C, int T, const float* gamma,
-                const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st) {
-    adain_coef_kernel<<<(C + 7) / 8, dim3(8, 128), 0, st>>>(stats, parts, ld, col0, C, T, gamma, beta, nw, nb,
-                                                             coef);
+                const float* beta, const float* nw, const float* nb, float* coef, cudaStream_t st, AdaSegs seg) {
+    adain_coef_kernel<<<dim3((C + 7) / 8, seg.p0 ? seg.n : 1), dim3(8, 128), 0, st>>>(
+        stats, parts, ld, col0, C, T, gamma, beta, nw, nb, coef, seg);
 }
 
 void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_part, float* stats,
-               cudaStream_t st) {
+               cudaStream_t st, const int* part_rows) {
     const int parts = (T + rows_per_part - 1) / rows_per_part;
     dim3 grid((ncols + 31) / 32, parts);
-    col_stats_kernel<<<grid, dim3(32, 8), 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats);
+    col_stats_kernel<<<grid, dim3(32, 8), 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats, part_rows);
 }
 
 void f0n_down(const float* f0, const float* n, const float* wf, const float* bf, const float* wn, const float* bn,
@@ -403,15 +431,16 @@ void concat_cols(float* dst, int ld, int col0, int T, const float* a, int lda, i
 }
 
 void dw_upsample_pack(const float* x, int ldx, int T, int C, const float* scale, const float* shift, float slope,
-                      const float* w, const float* b, void* hi, void* lo, int Cp, bool split, cudaStream_t st) {
+                      const float* w, const float* b, void* hi, void* lo, int Cp, bool split, cudaStream_t st,
+                      SegRows sr, int cstride) {
     const long total = (long)2 * T * Cp;
     const int g = nblocks(total, 256);
     if (small_index(total)) {
-        if (split) dw_upsample_pack_kernel<true, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
-        else dw_upsample_pack_kernel<false, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+        if (split) dw_upsample_pack_kernel<true, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp, sr, cstride);
+        else dw_upsample_pack_kernel<false, int><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp, sr, cstride);
     } else {
-        if (split) dw_upsample_pack_kernel<true, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
-        else dw_upsample_pack_kernel<false, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp);
+        if (split) dw_upsample_pack_kernel<true, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp, sr, cstride);
+        else dw_upsample_pack_kernel<false, long><<<g, 256, 0, st>>>(x, ldx, T, C, scale, shift, slope, w, b, hi, lo, Cp, sr, cstride);
     }
 }
 

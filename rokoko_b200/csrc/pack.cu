@@ -31,8 +31,8 @@ __device__ __forceinline__ float snake_sin(float x) {
     return __sinf(r);
 }
 
-__device__ __forceinline__ float act_transform(float v, int c, const PackArgs& a) {
-    if (a.scale) v = a.scale[c] * v + a.shift[c];
+__device__ __forceinline__ float act_transform(float v, int c, const PackArgs& a, int seg) {
+    if (a.scale) v = a.scale[(size_t)seg * a.coef_stride + c] * v + a.shift[(size_t)seg * a.coef_stride + c];
     if (a.snake) {
         const float al = a.snake[c];
         const float s = snake_sin(al * v);
@@ -51,6 +51,8 @@ __global__ void pack_act_kernel(PackArgs a) {
     for (I idx = (I)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (I)gridDim.x * blockDim.x) {
         const int q = (int)(idx / groups);
         const int g = (int)(idx - (I)q * groups);
+        int seg = 0;
+        if (a.part_seg) seg = (q & 63) < a.part_rows[q >> 6] ? a.part_seg[q >> 6] : -1;
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
@@ -58,9 +60,9 @@ __global__ void pack_act_kernel(PackArgs a) {
             const int r = cd / a.C;            // sub-row within the super-row
             const int c = cd - r * a.C;        // source channel
             float x = 0.0f;
-            if (r < a.sr_stride) {
+            if (r < a.sr_stride && seg >= 0) {
                 const int row = q * a.sr_stride - a.sr_pad + r;
-                if (row >= 0 && row < a.rows_src) x = act_transform(a.x[(long)row * a.ldx + c], c, a);
+                if (row >= 0 && row < a.rows_src) x = act_transform(a.x[(long)row * a.ldx + c], c, a, seg);
             }
             v[j] = x;
         }
@@ -99,13 +101,15 @@ __global__ void pack_act_vec_kernel(PackArgs a) {
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
         const int q = idx / groups;
         const int g = idx - q * groups;
+        int seg = 0;
+        if (a.part_seg) seg = (q & 63) < a.part_rows[q >> 6] ? a.part_seg[q >> 6] : -1;
         float v[8];
-        if (g < cgroups && q < a.rows_src) {
+        if (g < cgroups && q < a.rows_src && seg >= 0) {
             load8(a.x + (size_t)q * a.ldx, g * 8, v);
             if (a.scale) {
                 float sc[8], sh[8];
-                load8(a.scale, g * 8, sc);
-                load8(a.shift, g * 8, sh);
+                load8(a.scale + (size_t)seg * a.coef_stride, g * 8, sc);
+                load8(a.shift + (size_t)seg * a.coef_stride, g * 8, sh);
 #pragma unroll
                 for (int j = 0; j < 8; j++) v[j] = sc[j] * v[j] + sh[j];
             }
@@ -266,7 +270,9 @@ int grid_for(long work, int threads) {
 }  // namespace
 
 cudaError_t pack_act(const PackArgs& a, bool split, cudaStream_t st) {
-    if ((a.Cp & 63) || a.sr_stride < 1) return cudaErrorInvalidValue;
+    if ((a.Cp & 63) || a.sr_stride < 1 || (a.part_seg && (a.sr_stride != 1 || !a.part_rows)) ||
+        (a.part_seg && a.scale && (a.coef_stride & 3)))
+        return cudaErrorInvalidValue;
     const long total = (long)a.rows_dst * (a.Cp >> 3);
     if (total == 0) return cudaSuccess;
     auto al16 = [](const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };

@@ -24,6 +24,12 @@ struct PackArgs {
     const float* snake;   // Snake alpha per channel (nullable)
     float slope;          // LeakyReLU slope
     int lrelu;            // apply LeakyReLU
+    // segmented rows (sr_stride 1 only): destination row q of part q/64 is valid
+    // when q % 64 < part_rows[q/64] and then uses the scale / shift of segment
+    // part_seg[q/64] (at + seg * coef_stride); other rows are written as zeros
+    const int* part_seg;
+    const int* part_rows;
+    int coef_stride;
 };
 
 // split = bf16 hi/lo; otherwise one fp16 plane.

@@ -34,6 +34,9 @@ class rk_options(ctypes.Structure):
     _fields_ = [("precision", ctypes.c_int), ("max_tokens", ctypes.c_int), ("l_bucket", ctypes.c_int)]
 
 
+# rk_pcm_fn: int (*)(void* user, int index, const float* pcm, size_t n_samples)
+PCM_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float), ctypes.c_size_t)
+
 # (name, restype, argtypes) for every entry point of include/rk_b200.h
 SIGNATURES = [
     ("rk_status_string", ctypes.c_char_p, [ctypes.c_int]),
@@ -64,6 +67,8 @@ SIGNATURES = [
       ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     ("rk_encode", ctypes.c_int,
      [ctypes.c_void_p, _i32p, _i32p, ctypes.c_int, _f32p, _i32p, _i32p, _i32p]),
+    ("rk_synthesize_stream", ctypes.c_int,
+     [ctypes.c_void_p, _i32p, _i32p, ctypes.c_int, _f32p, _i32p, ctypes.c_int, PCM_FN, ctypes.c_void_p]),
     ("rk_decode", ctypes.c_int,
      [ctypes.c_void_p, _f32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_int)]),
     ("rk_get_stage", ctypes.c_int,

@@ -15,18 +15,19 @@ PCM back in the original order.
   front half; a bucket larger than a fair share is split so that one bucket
   cannot leave the other ranks idle.
 * Gather: with one process per GPU (torchrun) the ranks exchange only
-  (utterance, sample count) over the host process group; when they share one
-  host, rank 0 maps one node-local file of the total size (/dev/shm) and every
-  rank writes its PCM at its utterances' offsets (original order), so the
-  samples cross no socket.  Ranks on different hosts fall back to a pickled
-  gather over the process group.  With one process and one host thread per
+  (utterance, sample count) over the host process group; rank 0 sizes one
+  node-local file of the total (in $RK_GATHER_DIR, else /dev/shm) and writes a
+  random token beside it; when every rank reads the token back (they share the
+  file system, whatever their host names say), the other ranks write their PCM
+  at their utterances' offsets (original order) and rank 0 keeps its own
+  arrays, so no sample crosses a socket.  Otherwise every rank falls back to a
+  pickled gather over the process group.  With one process and one host thread per
   GPU the threads write into a shared list.  Nothing here is a device
   collective.
 """
 from __future__ import annotations
 
 import os
-import socket
 import tempfile
 import threading
 import uuid
@@ -105,6 +106,9 @@ def run_rank(synth: Callable[[int], np.ndarray], indices: Sequence[int]) -> list
 
 
 def _shm_dir() -> str:
+    d = os.environ.get("RK_GATHER_DIR")
+    if d:
+        return d
     return "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else tempfile.gettempdir()
 
 
@@ -123,16 +127,17 @@ def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) ->
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     meta = [None] * world
-    dist.all_gather_object(meta, (socket.gethostname(), [(int(i), int(p.shape[0])) for i, p in local]), group=group)
+    dist.all_gather_object(meta, [(int(i), int(p.shape[0])) for i, p in local], group=group)
     lengths = [-1] * n_total
-    for _, part in meta:
+    for part in meta:
         for i, n in part:
             lengths[i] = n
     missing = [i for i, n in enumerate(lengths) if n < 0]
     if missing:
         raise RuntimeError(f"gather_pcm: no PCM for utterances {missing[:8]}")
-    if len({h for h, _ in meta}) == 1:
-        return _gather_shared_file(local, lengths, rank, group)
+    done, out = _gather_shared_file(local, lengths, rank, world, group)
+    if done:
+        return out
     bucket = [None] * world if rank == 0 else None
     dist.gather_object(local, bucket, dst=0, group=group)
     if rank != 0:
@@ -144,24 +149,42 @@ def gather_pcm(local: list[tuple[int, np.ndarray]], n_total: int, group=None) ->
     return out
 
 
-def _gather_shared_file(local, lengths: list[int], rank: int, group) -> list[np.ndarray] | None:
+def _gather_shared_file(local, lengths: list[int], rank: int, world: int, group):
     """Node-local gather: rank 0 sizes a file for every sample (float32, original
-    order), each rank writes its own utterances at their offsets with pwrite,
-    and rank 0 maps the file copy-on-write and removes its name (the mapping
-    outlives it), so the returned arrays are views with no copy back."""
+    order) and writes a random token beside it; if every rank reads the token
+    back they share the file, the other ranks write their utterances at their
+    offsets with pwrite, and rank 0 maps the file copy-on-write (its name removed
+    once mapped) and keeps its own arrays.  Returns (True, PCM list on rank 0 /
+    None elsewhere), or (False, None) on every rank when some rank cannot see
+    the file (the caller then gathers over the process group)."""
     import torch.distributed as dist
     offsets = np.zeros(len(lengths) + 1, np.int64)
     np.cumsum(np.asarray(lengths, np.int64), out=offsets[1:])
     total = int(offsets[-1])
-    name = [None]
+    info = [None, None]
     if rank == 0:
-        name[0] = os.path.join(_shm_dir(), f"rk_pcm_{os.getpid()}_{uuid.uuid4().hex}")
-        with open(name[0], "wb") as f:
+        info[0] = f"rk_pcm_{os.getpid()}_{uuid.uuid4().hex}"
+        info[1] = uuid.uuid4().hex
+    dist.broadcast_object_list(info, src=0, group=group)
+    name, token = info
+    path = os.path.join(_shm_dir(), name)  # every rank looks in its own node-local directory
+    if rank == 0:
+        with open(path, "wb") as f:
             f.truncate(max(total, 1) * 4)
-    dist.broadcast_object_list(name, src=0, group=group)
-    path = name[0]
+        with open(path + ".id", "w") as f:
+            f.write(token)
+    dist.barrier(group=group)
     try:
-        if local and total:
+        with open(path + ".id") as f:
+            sees = f.read() == token
+    except OSError:
+        sees = False
+    seen = [None] * world
+    dist.all_gather_object(seen, sees, group=group)
+    try:
+        if not all(seen):
+            return False, None
+        if rank != 0 and local and total:
             fd = os.open(path, os.O_WRONLY)
             try:
                 for i, pcm in local:
@@ -174,17 +197,19 @@ def _gather_shared_file(local, lengths: list[int], rank: int, group) -> list[np.
                 os.close(fd)
         dist.barrier(group=group)
         if rank != 0:
-            return None
+            return True, None
+        mine = {int(i): np.asarray(p, np.float32).reshape(-1) for i, p in local}
         if total == 0:
-            return [np.zeros(0, np.float32) for _ in lengths]
+            return True, [np.zeros(0, np.float32) for _ in lengths]
         flat = np.memmap(path, dtype=np.float32, mode="c", shape=(total,))
-        return [flat[offsets[i]:offsets[i + 1]] for i in range(len(lengths))]
+        return True, [mine[i] if i in mine else flat[offsets[i]:offsets[i + 1]] for i in range(len(lengths))]
     finally:
         if rank == 0:
-            try:
-                os.remove(path)
-            except FileNotFoundError:
-                pass
+            for f in (path, path + ".id"):
+                try:
+                    os.remove(f)
+                except FileNotFoundError:
+                    pass
 
 
 def run_threads(synths: Sequence[Callable[[int], np.ndarray]], items: Sequence[Unit]) -> list[np.ndarray]:

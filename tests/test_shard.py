@@ -55,10 +55,22 @@ def _gloo_worker(rank, world, port, q, other_host=False, n_utts=None):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     if other_host and rank == 1:
-        # this rank claims another host: the gather must take the pickled path
-        shard.socket.gethostname = lambda: "another-host"
+        # this rank's node-local directory is not rank 0's (as on another host, even
+        # under the same host name): it cannot read the token, so the gather must
+        # take the pickled path
+        import tempfile
+        os.environ["RK_GATHER_DIR"] = tempfile.mkdtemp()
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    used_file = []
+    orig = shard._gather_shared_file
+
+    def spy(*a, **k):
+        r = orig(*a, **k)
+        used_file.append(r[0])
+        return r
+
+    shard._gather_shared_file = spy
     try:
         utts = configs.config2(seed=7)[:n_utts]
         items = shard.units(utts)
@@ -66,15 +78,15 @@ def _gloo_worker(rank, world, port, q, other_host=False, n_utts=None):
         local = shard.run_rank(lambda i: np.full(600 * items[i].L, i, np.float32), mine)
         out = shard.gather_pcm(local, len(items))
         if rank == 0:
-            q.put([(p.shape[0], float(p[0])) for p in out])
+            q.put(([(p.shape[0], float(p[0])) for p in out], used_file[0]))
         else:
-            q.put(out)
+            q.put((out, used_file[0]))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("other_host,n_utts", [(False, None), (True, None), (False, 1)],
-                         ids=["one-host-file", "two-hosts-pickled", "one-utterance-idle-rank"])
+                         ids=["shared-file", "separate-dirs-pickled", "one-utterance-idle-rank"])
 def test_gather_pcm_over_gloo_world2(other_host, n_utts):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -87,7 +99,9 @@ def test_gather_pcm_over_gloo_world2(other_host, n_utts):
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0
-    got = [r for r in res if r is not None]
+    got = [r for r, _ in res if r is not None]
     assert len(got) == 1
+    # the shared file is used exactly when both ranks can read rank 0's token
+    assert [f for _, f in res] == [not other_host] * 2
     items = shard.units(configs.config2(seed=7)[:n_utts])
     assert got[0] == [(600 * u.L, float(u.index)) for u in items]

@@ -97,6 +97,7 @@ extern "C" void rk_destroy(rk_ctx* c) {
     if (c->side) cudaStreamSynchronize(c->side);
     c->pending.clear();
     free_decode_ws(c);
+    free_decode_batch_ws(c);
     free_front_ws(c);
     free_weights(c);
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
@@ -299,25 +300,22 @@ extern "C" size_t rk_compute_decode_bytes(int T, int L) {
 
 namespace {
 
-// Decoder + generator for one pending utterance: its stashed inputs into the
-// decode workspace, the decode graph for its bucket, PCM (600 L samples) to
-// `pcm` (host, may be null).
-rk_status decode_pending(rk_ctx* c, const rk_ctx::Pending& p, float* pcm, const char* who) {
-    rk_status s = ensure_decode_ws(c, p.L_b);
-    if (s) return s;
-    DecodeWS& w = c->ws;
-    cudaStream_t st = c->stream;
-    const size_t n_asr = (size_t)p.L_b * 512, n2 = (size_t)2 * p.L_b;
-    if (cudaMemcpyAsync(w.asr, p.asr, n_asr * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(w.f0, p.f0, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(w.n, p.n, n2 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
-        cudaMemcpyAsync(w.style, p.style, 128 * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, (std::string(who) + ": decoder inputs").c_str());
-    s = enqueue_decode(c, p.L_b);
-    if (s) return s;
-    const size_t n = (size_t)600 * p.L;
-    if (pcm && cudaMemcpyAsync(pcm, w.audio, n * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-        return fail_cuda(RK_ERR_CUDA, (std::string(who) + ": pcm download").c_str());
+// Decoder + generator for pending utterances [first, first + n): the decoder
+// blocks of up to kDecodeBatch of them per pass (decode_batch.cu), then each
+// one's generator graph; PCM (600 L samples each) to pcm[i] (host, may be null).
+constexpr int kDecodeBatch = 32;
+
+rk_status decode_entries(rk_ctx* c, size_t first, int n, float* const* pcm) {
+    for (int b0 = 0; b0 < n; b0 += kDecodeBatch) {
+        const int nb = std::min(kDecodeBatch, n - b0);
+        std::vector<PendingRef> refs(nb);
+        for (int i = 0; i < nb; i++) {
+            const rk_ctx::Pending& p = c->pending[first + b0 + i];
+            refs[i] = PendingRef{p.L, p.L_b, p.asr, p.f0, p.n, p.style};
+        }
+        rk_status s = decode_batch(c, refs.data(), nb, pcm ? pcm + b0 : nullptr);
+        if (s) return s;
+    }
     return RK_OK;
 }
 
@@ -338,12 +336,11 @@ extern "C" rk_status rk_infer(rk_ctx* c, const int32_t* tokens, int T, const flo
     rk_status s = encode_batch(c, tokens, &Tv, 1, style256, dur_override, dur_out, &L, "rk_infer");
     if (s) { cudaStreamSynchronize(c->stream); drop_pending(c, before); return s; }
     if (L_out) *L_out = L;
-    const rk_ctx::Pending p = c->pending.back();
     const size_t n = std::min((size_t)600 * (size_t)L, pcm_capacity);
     std::vector<float> tmp;
     float* dst = pcm;
     if (pcm && n < (size_t)600 * L) { tmp.resize((size_t)600 * L); dst = tmp.data(); }
-    s = decode_pending(c, p, dst, "rk_infer");
+    s = decode_entries(c, c->pending.size() - 1, 1, &dst);
     if (!s) s = check_device_error(c);
     else cudaStreamSynchronize(c->stream);
     drop_pending(c, before);
@@ -379,16 +376,15 @@ extern "C" rk_status rk_decode(rk_ctx* c, float* pcm, size_t pcm_capacity, size_
     size_t need = 0;
     for (auto& p : c->pending) need += (size_t)600 * p.L;
     if (pcm && pcm_capacity < need) return fail(RK_ERR_WORKSPACE, "rk_decode: pcm buffer smaller than 600 * sum(L)");
+    std::vector<float*> dst((size_t)B, nullptr);
     size_t off = 0;
-    rk_status s = RK_OK;
-    for (int b = 0; b < B && !s; b++) {
-        const rk_ctx::Pending& p = c->pending[b];
-        s = decode_pending(c, p, pcm ? pcm + off : nullptr, "rk_decode");
-        if (s) break;
-        const size_t n = (size_t)600 * p.L;
+    for (int b = 0; b < B; b++) {
+        const size_t n = (size_t)600 * c->pending[b].L;
+        if (pcm) dst[b] = pcm + off;
         if (n_samples) n_samples[b] = pcm ? n : 0;
         off += n;
     }
+    rk_status s = decode_entries(c, 0, B, dst.data());
     cudaStreamSynchronize(c->stream);
     drop_pending(c, 0);
     return s ? s : check_device_error(c);
@@ -476,14 +472,15 @@ extern "C" rk_status rk_synthesize_stream(rk_ctx* c, const int32_t* tokens, cons
         if (cudaStreamWaitEvent(c->stream, c->ev_enc[k & 1], 0) != cudaSuccess)
             return abort_all(fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event wait"));
         std::vector<size_t> n_of(nb), at(nb);
+        std::vector<float*> dst(nb);
         size_t off = 0;
-        for (int i = 0; i < nb && !s; i++) {
+        for (int i = 0; i < nb; i++) {
             at[i] = off;
             n_of[i] = (size_t)600 * c->pending[i].L;
-            s = decode_pending(c, c->pending[i], c->h_pcm[pb] + off, "rk_synthesize_stream");
+            dst[i] = c->h_pcm[pb] + off;
             off += n_of[i];
         }
-        if (s) return abort_all(s);
+        if ((s = decode_entries(c, 0, nb, dst.data()))) return abort_all(s);
         if (cudaEventRecord(c->ev_chunk, c->stream) != cudaSuccess)
             return abort_all(fail_cuda(RK_ERR_CUDA, "rk_synthesize_stream: event record"));
         // the next chunk's front half overlaps this chunk's decode (its own stream, its own buffers)

@@ -357,7 +357,9 @@ rk_status ensure_decode_ws(rk_ctx* c, int L) {
 
 // ---------------------------------------------------------------- forward
 // Inputs already in ws.asr [L][512], ws.f0 [2L], ws.n [2L], ws.style [128].
-static rk_status enqueue_decode_body(rk_ctx* c, int L) {
+// gen_only: the decoder blocks ran elsewhere (the batched pass of rk_decode) and
+// their output is already in ws.gx [2L][512]; the graph starts at the generator.
+static rk_status enqueue_decode_body(rk_ctx* c, int L, bool gen_only) {
     DecodeWS& w = c->ws;
     const DecoderW& d = c->dec;
     const int L2 = 2 * L, T1 = 20 * L, T2 = 120 * L + 1, TA = 600 * L;
@@ -401,6 +403,7 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
     if (!s.ok()) return s.status;
 
     // ---- decoder blocks (src/rokoko.cpp:921-990) on the main stream
+    if (!gen_only) {
     f0n_down(w.f0, w.n, d.f0_conv_w, d.f0_conv_b, d.n_conv_w, d.n_conv_b, w.f0d, w.nd, L, r.st);
     r.check_launch("f0n_down");
     concat_cols(w.cat514, 514, 0, L, w.asr, 512, 512, nullptr, 0, 0, w.f0d, w.nd, r.st);
@@ -430,6 +433,7 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
                  w.stats_in[bi + 1], 1090, d.fc);
     resblk1d(r, d.decode[3], w.in1090[3], 1090, w.stats_in[3], parts_L, 1090, L, w.gx, 512, nullptr, 0, d.fc);
     record(r, "dec_decode3", w.gx, (size_t)L2 * 512);
+    }
     // LeakyReLU(0.1) -> ups[0] operand
     pack(r, w.gx, 512, L2, 512, w.op_b, d.ups[0].Cp, sp, nullptr, nullptr, 0.1f, true);
     if (!r.ok()) return r.status;
@@ -504,10 +508,10 @@ static rk_status enqueue_decode_body(rk_ctx* c, int L) {
 // a profiled decode (RK_PROFILE_CONV and / or RK_PROFILE_TIMELINE, optionally
 // RK_PROFILE_SERIAL) is captured into its own graph whose timing events are
 // event nodes, so that each replay re-records them.
-rk_status enqueue_decode(rk_ctx* c, int L) {
+rk_status enqueue_decode(rk_ctx* c, int L, bool gen_only) {
     const bool prof_graph = c->profile && (c->prof_mode & (RK_PROFILE_CONV | RK_PROFILE_TIMELINE));
-    if (c->record || (c->profile && !prof_graph) || !c->use_graphs) return enqueue_decode_body(c, L);
-    const std::pair<int, int> key{L, prof_graph ? c->prof_mode : 0};
+    if (c->record || (c->profile && !prof_graph) || !c->use_graphs) return enqueue_decode_body(c, L, gen_only);
+    const std::pair<int, int> key{L, (prof_graph ? c->prof_mode : 0) | (gen_only ? 0x100 : 0)};
     auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
         const long long before = c->launches;
@@ -518,7 +522,7 @@ rk_status enqueue_decode(rk_ctx* c, int L) {
         if (prof_graph) { flops0.swap(c->prof_flops); c->prof_used = 0; marks0.swap(c->tl_meta); }
         if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
             return fail_cuda(RK_ERR_CUDA, "graph capture begin");
-        rk_status s = enqueue_decode_body(c, L);
+        rk_status s = enqueue_decode_body(c, L, gen_only);
         cudaGraph_t g = nullptr;
         cudaError_t e = cudaStreamEndCapture(c->stream, &g);
         rk_ctx::GraphRec rec;

@@ -176,6 +176,20 @@ struct FrontWS {
     Operand op_p;
 };
 
+// The decoder blocks of a batch of pending utterances over their segmented
+// frames (capacity cap_R rows, cap_B utterances); see seg.h.
+struct DecBatchWS {
+    int cap_R = 0, cap_B = 0;
+    std::vector<void*> allocs;
+    float *asr = nullptr, *f0 = nullptr, *n = nullptr, *style = nullptr, *fc = nullptr, *f0d = nullptr,
+          *nd = nullptr, *cat514 = nullptr, *asr_res = nullptr, *gx = nullptr;
+    float* in1090[4] = {nullptr, nullptr, nullptr, nullptr};
+    float *stats_cat = nullptr, *stats_in[4] = {nullptr, nullptr, nullptr, nullptr};
+    float *sc = nullptr, *r1 = nullptr, *coef = nullptr, *stats_a = nullptr;
+    int* layout = nullptr;
+    Operand op;
+};
+
 struct StageRec {  // captured stage activations (rk_record_stages)
     std::vector<float> data;
 };
@@ -220,6 +234,7 @@ struct rk_ctx {
     bool has_front = false;
     rk::DecodeWS ws;
     rk::FrontWS fws;
+    rk::DecBatchWS dws;
     bool record = false;
     std::map<std::string, rk::StageRec> stages;
     long long launches = 0;

@@ -34,6 +34,12 @@ int nblocks(long work, int threads, int cap = 148 * 16) {
     return (int)(b < 1 ? 1 : b);
 }
 
+// segment of row r of a segmented layout, -1 for a gap row
+__device__ __forceinline__ int seg_of_row(const SegRows& sr, int r) {
+    const int p = r >> 6;
+    return (r & 63) < sr.part_rows[p] ? sr.part_seg[p] : -1;
+}
+
 // element counts for which a 32-bit grid-stride index cannot overflow
 bool small_index(long total) { return total < (1L << 31) - 148L * 16 * 1024; }
 
@@ -174,6 +180,31 @@ __global__ void f0n_down_kernel(const float* __restrict__ f0, const float* __res
     nd[t] = b + bn[0];
 }
 
+// Segmented form over the rows of a batch: row r of utterance u (base layout,
+// offset off_u = 64 * p0[u]) reads F0 / N at x2 rows [2 off_u, 2 off_u + 2 n_u);
+// gap rows are written as zeros.
+__global__ void f0n_down_seg_kernel(const float* __restrict__ f0, const float* __restrict__ n,
+                                    const float* __restrict__ wf, const float* __restrict__ bf,
+                                    const float* __restrict__ wn, const float* __restrict__ bn, float* f0d,
+                                    float* nd, int R, SegRows sr, AdaSegs as) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int u = seg_of_row(sr, r);
+    if (u < 0) { f0d[r] = 0.f; nd[r] = 0.f; return; }
+    const int off = 64 * as.p0[u], len = as.T[u];
+    const int t = r - off;
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < 3; k++) {
+        const int ti = 2 * t - 1 + k;
+        if (ti >= 0 && ti < 2 * len) {
+            a += wf[k] * f0[2 * off + ti];
+            b += wn[k] * n[2 * off + ti];
+        }
+    }
+    f0d[r] = a + bf[0];
+    nd[r] = b + bn[0];
+}
+
 // I = int when the element count leaves room for the grid stride below 2^31
 // (32-bit division), long otherwise.
 template <typename I>
@@ -197,10 +228,6 @@ __global__ void concat_cols_kernel(float* dst, int ld, int col0, int T, const fl
 // written as zeros, inputs outside the row's segment count as zeros (the
 // utterance's own boundary), and the AdaIN coefficients of segment u sit at
 // scale + u * cstride.
-__device__ __forceinline__ int seg_of_row(const SegRows& sr, int r) {
-    const int p = r >> 6;
-    return (r & 63) < sr.part_rows[p] ? sr.part_seg[p] : -1;
-}
 
 template <bool SPLIT, typename I>
 __global__ void dw_upsample_pack_kernel(const float* __restrict__ x, int ldx, int T, int C,
@@ -414,6 +441,11 @@ void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_
     const int parts = (T + rows_per_part - 1) / rows_per_part;
     dim3 grid((ncols + 31) / 32, parts);
     col_stats_kernel<<<grid, dim3(32, 8), 0, st>>>(x, ld, col0, ncols, T, rows_per_part, parts, stats, part_rows);
+}
+
+void f0n_down_seg(const float* f0, const float* n, const float* wf, const float* bf, const float* wn,
+                  const float* bn, float* f0d, float* nd, int R, SegRows sr, AdaSegs as, cudaStream_t st) {
+    f0n_down_seg_kernel<<<(R + 255) / 256, 256, 0, st>>>(f0, n, wf, bf, wn, bn, f0d, nd, R, sr, as);
 }
 
 void f0n_down(const float* f0, const float* n, const float* wf, const float* bf, const float* wn, const float* bn,

@@ -49,6 +49,10 @@ void col_stats(const float* x, int ld, int col0, int ncols, int T, int rows_per_
 void f0n_down(const float* f0, const float* n, const float* wf, const float* bf, const float* wn,
               const float* bn, float* f0d, float* nd, int L, cudaStream_t st);
 
+// The same over the segmented rows of a batch (base layout R rows; F0 / N in the x2 layout).
+void f0n_down_seg(const float* f0, const float* n, const float* wf, const float* bf, const float* wn,
+                  const float* bn, float* f0d, float* nd, int R, SegRows sr, AdaSegs as, cudaStream_t st);
+
 // dst[t, :] = [a[t, 0:ca] | b[t, 0:cb] | c[t] | d[t]] into columns [col0, ...) of a row of length ld.
 void concat_cols(float* dst, int ld, int col0, int T, const float* a, int lda, int ca, const float* b, int ldb,
                  int cb, const float* c, const float* d, cudaStream_t st);

@@ -238,7 +238,7 @@ def decoder_record(dev, steps: int, warmup: int, flush):
     profiling graph, e2e through rk_decode_features with host buffers."""
     import torch
     from rokoko_b200 import configs, koko
-    from rokoko_b200.context import FP32, RK_PROFILE_CONV, RK_PROFILE_SERIAL, Context
+    from rokoko_b200.context import FP32, RK_PROFILE_CONV, RK_PROFILE_SERIAL, RK_PROFILE_TIMELINE, Context
     blob = koko.random_v1_blob(0)
     ctx = Context(dev.index, FP32)
     ctx.load_weights(blob)
@@ -288,6 +288,13 @@ def decoder_record(dev, steps: int, warmup: int, flush):
             ctx.profile_read()
             serial_ms += ps0.elapsed_time(ps1)
     conv_ms, conv_flops, conv_n = ctx.profile_read()
+    # per-launch device times of one more serial decode (an event node after every launch)
+    ctx.profile(RK_PROFILE_TIMELINE | RK_PROFILE_SERIAL)
+    step()
+    ctx.profile_timeline()
+    flush.zero_()
+    step()
+    timeline = ctx.profile_timeline()
     ctx.profile(False)
     # end to end through the host-buffer call
     h = [torch.from_numpy(a).pin_memory().numpy() for a in (c.asr, c.f0, c.n, c.style)]
@@ -307,11 +314,53 @@ def decoder_record(dev, steps: int, warmup: int, flush):
                 "h2d_bytes_per_step": int(sum(a.nbytes for a in (c.asr, c.f0, c.n, c.style))),
                 "d2h_bytes_per_step": int(pcm.nbytes)},
         "_conv": (conv_ms / steps, conv_flops / steps, conv_n, serial_ms / steps, t_ms / steps),
+        "_timeline": timeline,
     }
+
+
+def conv_shapes(timeline, peak_tflops, hbm_gbs, planes=2):
+    """One row per conv shape of a serial profiled decode: launches, device ms (between the
+    event nodes around each launch), algorithmic TFLOP/s and the shape's own roofline
+    min(P_eff, I * BW).  The FP32 semantics (planes = 2, hi / lo) issue 3 bf16 products per
+    algorithmic product, so P_eff = burst bf16 peak / 3; FP16 weights (planes = 1) P_eff = peak.
+    I = FLOPs / bytes with bytes = the 16-bit operand planes and weights read once, the FP32
+    output written once and the FP32 residual read once when the conv adds one."""
+    p_eff = peak_tflops / (3.0 if planes == 2 else 1.0)
+    rows = {}
+    prev = 0.0
+    for _sid, name, t in timeline:
+        dt, prev = t - prev, t
+        if not name.startswith("conv "):
+            continue
+        tok = name.split()
+        cin, cout = (int(v) for v in tok[1].split(">"))
+        k, t_out = int(tok[2][1:]), int(tok[4][1:])
+        conv_t = "convT" in tok
+        i_t = tok.index("convT") + 1 if conv_t else -1
+        if conv_t and (i_t >= len(tok) or not tok[i_t].isdigit()):
+            continue  # a label without the input rows: FLOPs unknown
+        t_in = int(tok[i_t]) if conv_t else t_out
+        res = "res" in tok
+        cp = (cin + 63) // 64 * 64
+        fl = 2.0 * cin * cout * k * t_in
+        by = t_in * cp * 2 * planes + cout * k * cp * 2 * planes + t_out * cout * 4 * (2 if res else 1)
+        key = f"{cin}>{cout} K{k} T{t_out}" + (" convT" if conv_t else "") + (" res" if res else "")
+        r = rows.setdefault(key, [0, 0.0, 0.0, 0.0])
+        r[0] += 1; r[1] += dt; r[2] += fl; r[3] += by
+    out = []
+    for key, (n, ms, fl, by) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+        ach = fl / (ms * 1e-3) / 1e12 if ms > 0 else 0.0
+        inten = fl / by
+        bound = min(p_eff, inten * hbm_gbs / 1e3)
+        out.append({"shape": key, "launches": n, "ms": round(ms, 4), "tflops": round(ach, 1),
+                    "flop_per_byte": round(inten, 1), "bound_tflops": round(bound, 1),
+                    "bound": "tensor" if bound == p_eff else "hbm", "frac_of_bound": round(ach / bound, 3)})
+    return out
 
 
 def roofline_from(dec, peaks, src):
     conv_ms, conv_flops, conv_n, serial_ms, step_ms = dec.pop("_conv")
+    timeline = dec.pop("_timeline", None)
     peak = float(peaks.get("bf16_tflops"))
     achieved = conv_flops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else 0.0
     traffic = None
@@ -333,6 +382,7 @@ def roofline_from(dec, peaks, src):
         "conv_share_of_serial_step": round(conv_ms / serial_ms, 4) if serial_ms > 0 else None,
         "step_ms": round(step_ms, 4),
         "workload": "config-1 decoder (L = 400, FP32 semantics) on rank 0",
+        "conv_shapes": conv_shapes(timeline, peak, float(peaks.get("hbm_gbs"))) if timeline else None,
     }
 
 
@@ -412,8 +462,10 @@ def run_ours(args, world, rank, local):
     phase = []
     t0 = time.perf_counter()
     ev0.record()
+    torch.cuda.nvtx.range_push("timed")  # ncu --nvtx --nvtx-include timed/ profiles these steps only
     local_pcm = boxbench.run_batches(ctxs, utts, timed, phase)
     torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize(dev)
     t_rank = time.perf_counter() - t0

@@ -119,9 +119,12 @@ void conv(Run& r, const ConvCall& cc) {
     if (e1) cudaEventRecordWithFlags(e1, r.st, cudaEventRecordExternal);
     r.c->launches += nk;
     if (c->profile && (c->prof_mode & RK_PROFILE_TIMELINE)) {
+        // "conv C_in>C_out K d T_out [convT T_in] [res]": the shape a reader needs for the
+        // conv's FLOPs and bytes (res: a residual tensor is read)
         char nm[96];
-        snprintf(nm, sizeof nm, "conv %d>%d K%d d%d T%d%s", w.C_in, w.C_out, w.K, cc.dil, cc.T_out,
-                 w.phases > 1 ? " convT" : "");
+        int n = snprintf(nm, sizeof nm, "conv %d>%d K%d d%d T%d", w.C_in, w.C_out, w.K, cc.dil, cc.T_out);
+        if (w.phases > 1) n += snprintf(nm + n, sizeof nm - n, " convT %d", cc.rows_in);
+        if (cc.res) snprintf(nm + n, sizeof nm - n, " res");
         tl_mark(c, r.st, nm);
     }
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "conv_tc", e);

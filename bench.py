@@ -318,6 +318,70 @@ def decoder_record(dev, steps: int, warmup: int, flush):
     }
 
 
+def g2p_record(dev, steps: int, warmup: int, n_texts: int = 256, cpu_sample: int = 0):
+    """Neural phonemizer (rk_g2p_infer, G2P3 model of the reference's shape: d 256,
+    8 layers, 4 heads, SwiGLU 1024, 3x upsample; seeded random weights) on a batch of
+    `n_texts` seeded synthetic sentences (~121 characters, the reference corpus's
+    mean): host UTF-8 texts in, IPA strings out, per call.  value = input characters
+    per second (CUDA events around the calls on the context stream); e2e = wall
+    clock of the same calls.  cpu_sample > 0: the CPU restatement (oracle) on that
+    many of the texts."""
+    import torch
+    from rokoko_b200 import g2pfile
+    from rokoko_b200.g2p import G2PModel
+    blob = g2pfile.random_blob(0)
+    texts = g2pfile.random_texts(n_texts, seed=17)
+    chars = sum(len(t) for t in texts)
+    m = G2PModel(dev.index)
+    if not m.load_bytes(blob):
+        raise RuntimeError("G2P load failed")
+    for _ in range(warmup):
+        m.infer_batch(texts)
+    ext = torch.cuda.ExternalStream(m.ctx.stream, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    e0.record(ext)
+    for _ in range(steps):
+        m.infer_batch(texts)
+    e1.record(ext)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    m.ctx.kernel_count(reset=True)
+    m.infer_batch(texts)
+    launches = m.ctx.kernel_count()
+    m.close()
+    cfg = g2pfile.G2PConfig()
+    d, ff = cfg.d, cfg.ff
+    # algorithmic FLOPs of one call: the linears per character, attention per text (QK^T and PV)
+    per_char = cfg.n_layers * 2 * (4 * d * d + 3 * ff * d) + 2 * d * cfg.up * d + cfg.up * 2 * d * cfg.n_phones
+    flops = sum(len(t) * per_char + cfg.n_layers * 4 * len(t) ** 2 * d for t in texts)
+    peaks, src = measured_peaks()
+    tflops = flops * steps / (ms / 1000.0) / 1e12
+    rec = {"workload": f"G2P3 phonemizer, {n_texts} seeded synthetic sentences per call ({chars} characters), "
+                       "FP32 semantics", "value": round(chars * steps / (ms / 1000.0), 1), "unit": "chars/s",
+           "ms_per_call": round(ms / steps, 3), "steps": steps, "launches_per_call": launches,
+           "tflops_algorithmic": round(tflops, 1),
+           "frac_of_split_peak": round(3 * tflops / float(peaks["bf16_tflops"]), 4),
+           "peak_note": f"3 bf16 products per FP32-semantics product against bf16_tflops (burst) of {src}",
+           "e2e": {"value": round(chars * steps / wall, 1), "unit": "chars/s",
+                   "h2d_bytes_per_step": 8 * chars + 8 * n_texts, "d2h_bytes_per_step": 12 * chars}}
+    if cpu_sample > 0:
+        import oracle
+        o = oracle.G2POracle(blob)
+        sub = texts[:cpu_sample]
+        t0 = time.perf_counter()
+        for t in sub:
+            o.infer(t)
+        dt = time.perf_counter() - t0
+        o.close()
+        rec["cpu_baseline"] = {"value": round(sum(len(t) for t in sub) / dt, 1), "unit": "chars/s",
+                               "cores": host_threads(), "kind": "port",
+                               "sample": f"{cpu_sample} of the texts through the CPU restatement (oracle/g2p.cpp)"}
+    return rec
+
+
 def conv_shapes(timeline, peak_tflops, hbm_gbs, planes=2):
     """One row per conv shape of a serial profiled decode: launches, device ms (between the
     event nodes around each launch), algorithmic TFLOP/s and the shape's own roofline
@@ -505,10 +569,13 @@ def run_ours(args, world, rank, local):
               for b in timed) / len(timed)
 
     decoder = None
+    g2p = None
     if rank == 0:
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
         decoder = decoder_record(dev, max(3, min(args.steps, 20)), max(3, args.warmup), flush)
         del flush
+        g2p = g2p_record(dev, max(3, min(args.steps, 20)), 3,
+                         cpu_sample=0 if (world > 1 or args.no_cpu_baseline) else 8)
     for ctx in ctxs:
         ctx.close()
 
@@ -558,6 +625,7 @@ def run_ours(args, world, rank, local):
             "roofline": roof,
             "cpu_baseline": cpu,
             "decoder": decoder,
+            "g2p": g2p,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

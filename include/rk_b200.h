@@ -188,6 +188,27 @@ RK_API rk_status rk_synthesize_stream(rk_ctx* ctx, const int32_t* tokens, const 
                                       const float* style, const int32_t* dur_override, int chunk,
                                       rk_pcm_fn on_pcm, void* user);
 
+/* Neural phonemizer (rokoko::G2PModelCuda, src/g2p.h:374-430; load
+ * src/g2p.h:442-640, infer :678-882): UTF-8 text -> IPA phones.  The G2P3
+ * model (RoPE + RMSNorm, heads of 64 dimensions) lives in the context beside
+ * (or without) its TTS weights and always computes with FP32 semantics.
+ * rk_g2p_load parses a G2P3 blob (RK_ERR_WEIGHTS on a malformed or
+ * unsupported file) and replaces any model loaded before.  rk_g2p_infer
+ * phonemizes n texts (texts[i], text_bytes[i] bytes each) in one pass on the
+ * device: the phones of text i are written to out back to back, out_len[i]
+ * bytes each; a text that is empty or longer than 2048 characters gives ""
+ * (the reference's rule).  When out_cap is short, out_len still receives every
+ * size and the call returns RK_ERR_WORKSPACE.  rk_g2p_frames copies the
+ * per-frame CTC ids of the last rk_g2p_infer (up * characters per text, texts
+ * in order, empty texts taking none; *n = their count; ids may be NULL to ask
+ * for the count).  rk_g2p_param_bytes = the model's FP32 parameter bytes. */
+RK_API rk_status rk_g2p_load(rk_ctx* ctx, const void* blob, size_t bytes);
+RK_API rk_status rk_g2p_infer(rk_ctx* ctx, const char* const* texts, const size_t* text_bytes, int n, char* out,
+                              size_t out_cap, size_t* out_len);
+RK_API rk_status rk_g2p_frames(rk_ctx* ctx, int32_t* ids, size_t cap, size_t* n);
+RK_API size_t rk_g2p_param_bytes(rk_ctx* ctx);
+RK_API void rk_g2p_free(rk_ctx* ctx);
+
 /* Stage activations of the last forward (names as the oracle's stage dumps);
  * copies min(count, cap) floats; *count = element count (0 if unknown). */
 RK_API rk_status rk_get_stage(rk_ctx* ctx, const char* name, float* host_dst, size_t cap, size_t* count);

@@ -27,6 +27,11 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int)
 
 
+def _has_g2p(path: str) -> bool:
+    with open(path, "rb") as f:
+        return b"og2p_forward" in f.read()
+
+
 def build(force: bool = False) -> str:
     if force or not os.path.exists(_LIB_PATH):
         subprocess.run(["make", "-C", _HERE, "-s"], check=True)
@@ -36,8 +41,8 @@ def build(force: bool = False) -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
-            build()
+        if not os.path.exists(_LIB_PATH) or not _has_g2p(_LIB_PATH):
+            build(force=True)
         L = ctypes.CDLL(_LIB_PATH)
         L.orc_load.restype = ctypes.c_void_p
         L.orc_load.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
@@ -68,6 +73,17 @@ def lib():
         L.orc_weight_norm.argtypes = [_f32p, _f32p, c_int, c_long, _f32p]
         L.orc_gelu.argtypes = [_f32p, c_long, _f32p]
         L.orc_softmax.argtypes = [_f32p, c_int, c_int, _f32p]
+        L.og2p_load.restype = ctypes.c_void_p
+        L.og2p_load.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_size_t]
+        L.og2p_free.argtypes = [ctypes.c_void_p]
+        L.og2p_dims.argtypes = [ctypes.c_void_p, _i32p]
+        L.og2p_ids.restype = c_int
+        L.og2p_ids.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, _i32p, ctypes.c_size_t]
+        L.og2p_forward.restype = c_long
+        L.og2p_forward.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, _f32p, ctypes.c_size_t,
+                                   _i32p, ctypes.c_size_t]
+        L.og2p_ctc.restype = c_long
+        L.og2p_ctc.argtypes = [ctypes.c_void_p, _i32p, c_long, ctypes.c_char_p, ctypes.c_size_t]
         _lib = L
     return _lib
 
@@ -274,3 +290,52 @@ def softmax(x):
     y = np.empty_like(x)
     lib().orc_softmax(_fp(x), x.shape[0], x.shape[1], _fp(y))
     return y
+
+
+class G2POracle:
+    """The CPU restatement of rokoko's G2P3 phonemizer (oracle/g2p.cpp) for one
+    G2P3 blob: ids, logits, per-frame argmax and the CTC string of a text."""
+
+    def __init__(self, blob: bytes):
+        err = ctypes.create_string_buffer(256)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._h = lib().og2p_load(buf, len(blob), err, 256)
+        if not self._h:
+            raise RuntimeError("G2P oracle load failed: " + err.value.decode())
+        dims = np.zeros(7, np.int32)
+        lib().og2p_dims(self._h, _ip(dims))
+        self.d, self.heads, self.n_layers, self.ff, self.up, self.n_chars, self.n_phones = (int(x) for x in dims)
+
+    def close(self):
+        if self._h:
+            lib().og2p_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def ids(self, text: str) -> np.ndarray:
+        b = text.encode("utf-8")
+        out = np.zeros(len(b) + 1, np.int32)
+        n = lib().og2p_ids(self._h, b, len(b), _ip(out), out.size)
+        return out[:n]
+
+    def forward(self, text: str) -> tuple[np.ndarray, np.ndarray]:
+        """(logits [T*up][n_phones], argmax ids [T*up]); empty for "" or > 2048 characters."""
+        b = text.encode("utf-8")
+        rows = (len(b) + 1) * self.up
+        logits = np.zeros(rows * self.n_phones, np.float32)
+        best = np.zeros(rows, np.int32)
+        n = lib().og2p_forward(self._h, b, len(b), _fp(logits), logits.size, _ip(best), best.size)
+        if n < 0:
+            raise RuntimeError("og2p_forward: buffer too small")
+        return logits[: n * self.n_phones].reshape(n, self.n_phones), best[:n]
+
+    def ctc(self, best: np.ndarray) -> str:
+        best = np.ascontiguousarray(best, np.int32)
+        cap = 4 * best.size + 4
+        out = ctypes.create_string_buffer(cap)
+        n = lib().og2p_ctc(self._h, _ip(best), best.size, out, cap)
+        return out.raw[:n].decode("utf-8")
+
+    def infer(self, text: str) -> str:
+        return self.ctc(self.forward(text)[1])

@@ -77,9 +77,11 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 def build_compat(force: bool = False) -> str:
     """librokoko_compat.so: the reference's C++ model seam (include/rokoko/weights.h)
-    on top of librokoko_b200.so, compiled with the system g++."""
+    and phonemizer class (include/rokoko/g2p.h) on top of librokoko_b200.so,
+    compiled with the system g++."""
     src = os.path.join(HERE, "cpp", "rokoko_compat.cpp")
-    hdrs = [os.path.join(INCLUDE, "rokoko", "weights.h"), os.path.join(INCLUDE, "rk_b200.h")]
+    hdrs = [os.path.join(INCLUDE, "rokoko", "weights.h"), os.path.join(INCLUDE, "rokoko", "g2p.h"),
+            os.path.join(INCLUDE, "rk_b200.h")]
     if not force and not _stale(COMPAT, [src, LIB] + hdrs):
         return COMPAT
     cuda = os.path.dirname(os.path.dirname(NVCC))

@@ -1,8 +1,11 @@
 // rokoko_compat.cpp -- the reference's C++ model seam (include/rokoko/weights.h)
 // implemented on the C ABI of librokoko_b200.so: Weights::load ->
 // rk_create + rk_load_weights_koko, rokoko_infer -> rk_infer (predicted
-// durations, L bucketed by 32 as src/rokoko_f16.cpp:797-802 does).
+// durations, L bucketed by 32 as src/rokoko_f16.cpp:797-802 does); and the
+// reference's phonemizer class (include/rokoko/g2p.h): G2PModelCuda::load ->
+// rk_create + rk_g2p_load, infer -> rk_g2p_infer.
 #include "weights.h"
+#include "g2p.h"
 
 #include <cstdio>
 #include <cstring>
@@ -134,5 +137,74 @@ bool write_wav(const std::string& path, const float* audio, int n_samples, int s
     write_wav_to_(f, audio, n_samples, sample_rate);
     return (bool)f;
 }
+
+// ------------------------------------------------------------------ G2PModelCuda
+
+bool G2PModelCuda::load(const char* path, cudaStream_t stream) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return false;
+    std::vector<char> blob((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    if (stream) cudaStreamSynchronize(stream);
+    if (!ctx_) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return false;
+        rk_options o{};
+        o.precision = RK_PRECISION_FP32;
+        if (rk_create(dev, &o, &ctx_) != RK_OK) {
+            ctx_ = nullptr;
+            return false;
+        }
+    }
+    if (rk_g2p_load(ctx_, blob.data(), blob.size()) != RK_OK) {
+        std::fprintf(stderr, "g2p: %s\n", rk_last_error());
+        return loaded_;  // a model loaded before stays in place
+    }
+    loaded_ = true;
+    return true;
+}
+
+std::vector<std::string> G2PModelCuda::infer_batch(const std::vector<std::string>& texts,
+                                                   cudaStream_t stream) const {
+    std::vector<std::string> res(texts.size());
+    if (!loaded_ || texts.empty()) return res;
+    if (stream) cudaStreamSynchronize(stream);
+    const int n = (int)texts.size();
+    std::vector<const char*> ptr(n);
+    std::vector<size_t> len(n), out_len(n);
+    size_t cap = 16;
+    for (int i = 0; i < n; i++) {
+        ptr[i] = texts[i].data();
+        len[i] = texts[i].size();
+        cap += 12 * texts[i].size();  // up to 3 phones of <= 4 bytes per input byte
+    }
+    std::vector<char> out(cap);
+    rk_status s = rk_g2p_infer(ctx_, ptr.data(), len.data(), n, out.data(), out.size(), out_len.data());
+    if (s == RK_ERR_WORKSPACE) {
+        size_t need = 16;
+        for (size_t l : out_len) need += l;
+        out.resize(need);
+        s = rk_g2p_infer(ctx_, ptr.data(), len.data(), n, out.data(), out.size(), out_len.data());
+    }
+    if (s != RK_OK) raise("G2PModelCuda::infer", s);
+    size_t off = 0;
+    for (int i = 0; i < n; i++) {
+        res[i].assign(out.data() + off, out_len[i]);
+        off += out_len[i];
+    }
+    return res;
+}
+
+std::string G2PModelCuda::infer(const std::string& text, cudaStream_t stream) const {
+    if (!loaded_) return "";
+    return infer_batch({text}, stream)[0];
+}
+
+void G2PModelCuda::free() {
+    if (ctx_) rk_destroy(ctx_);
+    ctx_ = nullptr;
+    loaded_ = false;
+}
+
+size_t G2PModelCuda::param_bytes() const { return ctx_ ? rk_g2p_param_bytes(ctx_) : 0; }
 
 }  // namespace rokoko

@@ -10,6 +10,7 @@
 
 #include "../../include/rk_b200.h"
 #include "decode.h"
+#include "g2p.h"
 #include "infer.h"
 #include "model.h"
 #include "status.h"
@@ -100,6 +101,7 @@ extern "C" void rk_destroy(rk_ctx* c) {
     free_decode_batch_ws(c);
     free_front_ws(c);
     free_weights(c);
+    free_g2p(c);
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     for (cudaEvent_t e : c->tl_events) cudaEventDestroy(e);
     for (cudaEvent_t e : {c->ev_chunk, c->ev_enc[0], c->ev_enc[1], c->ev_stage})

@@ -1,11 +1,13 @@
-// attention_tc.cu -- ALBERT self-attention on the tensor cores (tcgen05 / TMEM).
+// attention_tc.cu -- multi-head self-attention on the tensor cores (tcgen05 / TMEM).
 //
-// Reference: src/rokoko_f16.cpp:227-244 (batched GEMM Q K^T, softmax kernel
-// src/kernels.cu:189-225, batched GEMM P V) and src/rokoko.cpp:363-384:
-// S = Q K^T * 0.125 over 12 heads of 64, softmax over the keys (no mask),
-// O = P V, for every utterance of the batch (segments of the row layout).
+// ALBERT (src/rokoko_f16.cpp:227-244: batched GEMM Q K^T, softmax kernel
+// src/kernels.cu:189-225, batched GEMM P V; src/rokoko.cpp:363-384) and the
+// neural phonemizer (src/g2p.h:772-790): S = Q K^T / 8 per head of 64
+// dimensions, softmax over the keys (no mask), O = P V, for every sequence of
+// a batch (segments of the row layout).  QKV rows hold [Q | K | V] of `heads`
+// heads each ([rows][3 * 64 heads]); the output rows are [rows][64 heads].
 //
-// One CTA of 128 threads per (128-query tile, head, utterance):
+// One CTA of 128 threads per (128-query tile, head, sequence):
 //   1. Q [128 x 64] and, in chunks of 64 keys, K [64 x 64] are converted from
 //      the FP32 QKV rows into 16-bit planes in shared memory (the 128-byte
 //      swizzled K-major layout the MMA reads; FP32 semantics keep bf16 hi and
@@ -14,12 +16,16 @@
 //      N = 64 keys, K = 64 dims), chunks double-buffered behind mbarriers.
 //   2. Thread i owns query row i = TMEM lane i: it reads its scores straight
 //      from TMEM (tcgen05.ld), takes the row maximum, then per key chunk
-//      computes e = exp(0.125 s - max) (0 past the utterance's keys), adds it
-//      to the row sum and writes the row of E_c into shared memory; V_c is
+//      computes e = exp(s / 8 - max) (0 past the sequence's keys), adds it to
+//      the row sum and writes the row of E_c into shared memory; V_c is
 //      written transposed (dims x keys) beside it; the elected thread issues
-//      O += E_c V_c into TMEM columns 0..63 (the columns of chunk 0's scores,
-//      read before the first such MMA).
-//   3. O row / sum -> ctx.
+//      O += E_c V_c into TMEM.
+//   3. O row / sum -> output.
+// Up to 512 keys the scores of all keys sit in TMEM at once and O takes the
+// columns of chunk 0 once they are read.  Longer sequences run in key blocks
+// of 448 (seven chunks; O in columns 448..511): per block the running row
+// maximum is raised to the block's and O and the row sum are rescaled by
+// exp(old max - new max) before the block's E V products (online softmax).
 // The scores never leave the SM.  Every wait is bounded (ptx.cuh): a timeout
 // records an error code in the context's error word and the CTA finishes
 // without writing (the host reports RK_ERR_DEVICE_TIMEOUT).
@@ -96,9 +102,12 @@ __device__ __forceinline__ void mma_block(uint32_t d_tmem, uint32_t a_hi, uint32
     }
 }
 
+constexpr int BLOCK_CHUNKS = 7;      // key chunks per block beyond 512 keys
+constexpr uint32_t O_COL_BLOCKED = 448;  // O's TMEM columns when the keys run in blocks
+
 template <bool SPLIT>
 __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restrict__ qkv_all, SegMeta s,
-                                                           float* __restrict__ ctx_all, uint32_t* err) {
+                                                           float* __restrict__ ctx_all, int hid, uint32_t* err) {
     using C = AttCfg<SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -109,11 +118,15 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
     const int q0 = blockIdx.x * QT;
     if (q0 >= T) return;  // uniform over the CTA
     const int head = blockIdx.y;
-    const float* qkv = qkv_all + (size_t)s.off[blockIdx.z] * 2304;
+    const int ld = 3 * hid;  // QKV row pitch
+    const float* qkv = qkv_all + (size_t)s.off[blockIdx.z] * ld;
     const int tid = threadIdx.x, warp = tid >> 5;
     const int nch = (T + KC - 1) / KC;
+    const bool single = nch * KC <= 512;  // every key's score in TMEM at once
+    const int bch = single ? nch : BLOCK_CHUNKS;
+    const uint32_t o_col = single ? 0u : O_COL_BLOCKED;
     uint32_t ncols = 64;
-    while ((int)ncols < nch * KC) ncols <<= 1;
+    while ((int)ncols < (single ? nch * KC : 512)) ncols <<= 1;
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) { mbar_init(&s_bar[i], 1); mbar_init(&pv_bar[i], 1); }
@@ -129,7 +142,7 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
         uint8_t* qh = smem + C::Q_OFF;
         uint8_t* ql = qh + C::Q_PLANE;
         const int q = q0 + tid;
-        const float* src = qkv + (size_t)q * 2304 + head * HD;
+        const float* src = qkv + (size_t)q * ld + head * HD;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             float v[8];
@@ -152,64 +165,86 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
     const uint32_t q_hi = smem_u32(smem + C::Q_OFF), q_lo = q_hi + C::Q_PLANE;
     bool ok = true;
 
-    // ---- phase S: scores of every key chunk into TMEM columns [64c, 64c + 64)
-    for (int c = 0; c < nch; c++) {
-        const int buf = c & 1;
-        if (c >= 2 && !mbar_wait(&s_bar[buf], ((c - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
-        if (!__syncthreads_and(ok)) break;
-        uint8_t* kh = smem + C::K_OFF + buf * C::NPL * C::K_PLANE;
-        uint8_t* kl = kh + C::K_PLANE;
-        {   // key row t >> 1, dims [32 (t & 1), +32)
-            const int kr = tid >> 1, half = tid & 1;
-            const int key = c * KC + kr;
-            const float* src = qkv + (size_t)key * 2304 + 768 + head * HD + 32 * half;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float v[8];
-                if (key < T) {
-                    const float4 a = reinterpret_cast<const float4*>(src + 8 * j)[0];
-                    const float4 b = reinterpret_cast<const float4*>(src + 8 * j)[1];
-                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; i++) v[i] = 0.f;
-                }
-                put8<SPLIT>(kh, kl, sw_off(kr, 32 * half + 8 * j), v);
-            }
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t k_hi = smem_u32(kh), k_lo = k_hi + C::K_PLANE;
-            mma_block<SPLIT>(tmem + (uint32_t)(c * KC), q_hi, q_lo, k_hi, k_lo, idesc, false);
-            umma_commit(&s_bar[buf]);
-        }
-    }
-    if (tid == 0 && ok) umma_commit(&fin_bar);
-    if (ok && !mbar_wait(&fin_bar, 0, err, RK_DEV_TIMEOUT_ACC)) ok = false;
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-
     const uint32_t row_tmem = tmem + ((uint32_t)(warp * 32) << 16);
     float mx = -3.0e38f, sum = 0.f;
-    if (ok) {
-        // ---- pass A: row maximum of the scaled scores over the utterance's keys
-        for (int c = 0; c < nch; c++) {
+    int gs = 0, gp = 0;        // S and E V chunks issued so far (mbarrier phases)
+    uint32_t fin_n = 0;        // uses of fin_bar so far
+    for (int c0 = 0; c0 < nch && ok; c0 += bch) {
+        const int c1 = min(nch, c0 + bch);
+        // ---- phase S: scores of the block's key chunks into TMEM columns [64 (c - c0), +64)
+        for (int c = c0; c < c1; c++, gs++) {
+            const int buf = gs & 1;
+            if (gs >= 2 && !mbar_wait(&s_bar[buf], ((gs - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+            if (!__syncthreads_and(ok)) break;
+            uint8_t* kh = smem + C::K_OFF + buf * C::NPL * C::K_PLANE;
+            uint8_t* kl = kh + C::K_PLANE;
+            {   // key row t >> 1, dims [32 (t & 1), +32)
+                const int kr = tid >> 1, half = tid & 1;
+                const int key = c * KC + kr;
+                const float* src = qkv + (size_t)key * ld + hid + head * HD + 32 * half;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float v[8];
+                    if (key < T) {
+                        const float4 a = reinterpret_cast<const float4*>(src + 8 * j)[0];
+                        const float4 b = reinterpret_cast<const float4*>(src + 8 * j)[1];
+                        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) v[i] = 0.f;
+                    }
+                    put8<SPLIT>(kh, kl, sw_off(kr, 32 * half + 8 * j), v);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t k_hi = smem_u32(kh), k_lo = k_hi + C::K_PLANE;
+                mma_block<SPLIT>(tmem + (uint32_t)((c - c0) * KC), q_hi, q_lo, k_hi, k_lo, idesc, false);
+                umma_commit(&s_bar[buf]);
+            }
+        }
+        // the block's scores (and every earlier E V product) have landed
+        if (tid == 0 && ok) umma_commit(&fin_bar);
+        if (ok && !mbar_wait(&fin_bar, fin_n & 1u, err, RK_DEV_TIMEOUT_ACC)) ok = false;
+        fin_n++;
+        ok = __syncthreads_and(ok);
+        tc_fence_after();
+        if (!ok) break;
+        // ---- pass A: row maximum of the scaled scores over the block's keys
+        float bmx = mx;
+        for (int c = c0; c < c1; c++) {
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 float v[32];
-                tmem_ld32(row_tmem + (uint32_t)(c * KC + 32 * h), v);
+                tmem_ld32(row_tmem + (uint32_t)((c - c0) * KC + 32 * h), v);
 #pragma unroll
                 for (int j = 0; j < 32; j++)
-                    if (c * KC + 32 * h + j < T) mx = fmaxf(mx, v[j] * 0.125f);
+                    if (c * KC + 32 * h + j < T) bmx = fmaxf(bmx, v[j] * 0.125f);
             }
         }
-        // ---- pass B: e = exp(0.125 s - max) chunk by chunk, O += E_c V_c
-        for (int c = 0; c < nch; c++) {
-            const int buf = c & 1;
-            if (c >= 2 && !mbar_wait(&pv_bar[buf], ((c - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+        if (c0 > 0) {
+            // online softmax: O and the row sum so far to the new maximum (alpha = 1 when the
+            // block does not raise it).  The condition is uniform over the CTA: tcgen05.ld / st
+            // are .sync.aligned, every lane of a warp must execute them together.
+            const float alpha = expf(mx - bmx);
+            sum *= alpha;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float v[32];
+                tmem_ld32(row_tmem + o_col + (uint32_t)(32 * h), v);
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] *= alpha;
+                tmem_st32(row_tmem + o_col + (uint32_t)(32 * h), v);
+            }
+        }
+        mx = bmx;
+        // ---- pass B: e = exp(s / 8 - max) chunk by chunk, O += E_c V_c
+        for (int c = c0; c < c1; c++, gp++) {
+            const int buf = gp & 1;
+            if (gp >= 2 && !mbar_wait(&pv_bar[buf], ((gp - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
             if (!__syncthreads_and(ok)) break;
             uint8_t* eh = smem + C::E_OFF + buf * C::NPL * C::E_PLANE;
             uint8_t* el = eh + C::E_PLANE;
@@ -218,7 +253,7 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 float v[32];
-                tmem_ld32(row_tmem + (uint32_t)(c * KC + 32 * h), v);
+                tmem_ld32(row_tmem + (uint32_t)((c - c0) * KC + 32 * h), v);
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const float e = (c * KC + 32 * h + j < T) ? expf(v[j] * 0.125f - mx) : 0.f;
@@ -241,7 +276,7 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int key = c * KC + kh0 + 8 * g + i;
-                        w[i] = key < T ? qkv[(size_t)key * 2304 + 1536 + head * HD + d] : 0.f;
+                        w[i] = key < T ? qkv[(size_t)key * ld + 2 * hid + head * HD + d] : 0.f;
                     }
                     put8<SPLIT>(vh, vl, sw_off(d, kh0 + 8 * g), w);
                 }
@@ -253,24 +288,24 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
                 tc_fence_after();
                 const uint32_t e_hi = smem_u32(eh), e_lo = e_hi + C::E_PLANE;
                 const uint32_t v_hi = smem_u32(vh), v_lo = v_hi + C::V_PLANE;
-                mma_block<SPLIT>(tmem, e_hi, e_lo, v_hi, v_lo, idesc, c > 0);
+                mma_block<SPLIT>(tmem + o_col, e_hi, e_lo, v_hi, v_lo, idesc, gp > 0);
                 umma_commit(&pv_bar[buf]);
             }
         }
     }
     if (tid == 0 && ok) umma_commit(&fin_bar);
-    if (ok && !mbar_wait(&fin_bar, 1, err, RK_DEV_TIMEOUT_ACC)) ok = false;
+    if (ok && !mbar_wait(&fin_bar, fin_n & 1u, err, RK_DEV_TIMEOUT_ACC)) ok = false;
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok) {
         // ---- O / sum -> ctx (row q0 + t, columns head*64 ..)
         const int q = q0 + tid;
         const float inv = 1.0f / sum;
-        float* dst = ctx_all + ((size_t)s.off[blockIdx.z] + q) * 768 + head * HD;
+        float* dst = ctx_all + ((size_t)s.off[blockIdx.z] + q) * hid + head * HD;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             float v[32];
-            tmem_ld32(row_tmem + (uint32_t)(32 * h), v);
+            tmem_ld32(row_tmem + o_col + (uint32_t)(32 * h), v);
             if (q < T) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
@@ -303,10 +338,13 @@ cudaError_t attention_tc_init() {
     return e;
 }
 
-cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st) {
-    const dim3 grid((s.max_len + QT - 1) / QT, 12, s.n);
-    if (split) attention_tc_kernel<true><<<grid, 128, att_smem(true), st>>>(qkv, s, ctx, err);
-    else attention_tc_kernel<false><<<grid, 128, att_smem(false), st>>>(qkv, s, ctx, err);
+cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st,
+                         int heads) {
+    if (heads < 1 || s.n < 1 || s.max_len < 1) return heads < 1 ? cudaErrorInvalidValue : cudaSuccess;
+    const dim3 grid((s.max_len + QT - 1) / QT, heads, s.n);
+    const int hid = heads * HD;
+    if (split) attention_tc_kernel<true><<<grid, 128, att_smem(true), st>>>(qkv, s, ctx, hid, err);
+    else attention_tc_kernel<false><<<grid, 128, att_smem(false), st>>>(qkv, s, ctx, hid, err);
     return cudaGetLastError();
 }
 

@@ -50,7 +50,9 @@ void adaln_concat(const float* x, RowMeta m, const float* fc, int fc_stride, int
 // Scaled dot-product attention (12 heads of 64, no mask) within every segment,
 // on the tensor cores (attention_tc.cu): qkv [rows][2304] = [Q | K | V],
 // ctx [rows][768]; split = FP32 semantics (split-bf16 products), else fp16.
-cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st);
+// heads of 64 dimensions; QKV rows [3 * 64 heads], output rows [64 heads]
+cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st,
+                         int heads = 12);
 cudaError_t attention_tc_init();
 void durations(const float* proj, RowMeta m, float* dur_f, int* dur_i, cudaStream_t st);
 // Duration -> alignment for every utterance: a block-wide scan of its durations

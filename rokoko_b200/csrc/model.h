@@ -196,6 +196,10 @@ struct StageRec {  // captured stage activations (rk_record_stages)
 
 }  // namespace rk
 
+namespace rk {
+struct G2PState;  // g2p.h: the neural phonemizer of a context
+}
+
 // one timeline mark: the stream index and the launch name
 struct TlMarkRec {
     int stream;
@@ -284,4 +288,6 @@ struct rk_ctx {
     void* h_stage = nullptr;
     size_t h_stage_bytes = 0;
     cudaEvent_t ev_stage = nullptr;  // the last uploads out of h_stage are done
+    // the neural phonemizer (rk_g2p_load), independent of the TTS weights
+    rk::G2PState* g2p = nullptr;
 };

@@ -77,6 +77,14 @@ SIGNATURES = [
     ("rk_kernel_count", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_longlong), ctypes.c_int]),
     ("rk_stream", ctypes.c_void_p, [ctypes.c_void_p]),
     ("rk_compute_decode_bytes", ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ("rk_g2p_load", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]),
+    ("rk_g2p_infer", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_size_t), ctypes.c_int,
+      ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    ("rk_g2p_frames", ctypes.c_int,
+     [ctypes.c_void_p, _i32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    ("rk_g2p_param_bytes", ctypes.c_size_t, [ctypes.c_void_p]),
+    ("rk_g2p_free", None, [ctypes.c_void_p]),
     ("rk_profile", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     ("rk_profile_read", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),

@@ -16,14 +16,19 @@ PKG = os.path.join(ROOT, "rokoko_b200")
 CUDA = "/usr/local/cuda"
 
 
-def _compile(out_dir: str) -> str:
-    exe = os.path.join(out_dir, "rokoko_infer_main")
+def _compile_src(out_dir: str, name: str) -> str:
+    """g++ tests/cpp/<name>.cpp against include/rokoko and the compat library."""
+    exe = os.path.join(out_dir, name)
     cmd = ["/usr/bin/g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include", "rokoko"),
-           "-I", os.path.join(CUDA, "include"), os.path.join(ROOT, "tests", "cpp", "rokoko_infer_main.cpp"),
+           "-I", os.path.join(CUDA, "include"), os.path.join(ROOT, "tests", "cpp", name + ".cpp"),
            "-o", exe, "-L", PKG, "-lrokoko_compat", "-lrokoko_b200", "-L", os.path.join(CUDA, "lib64"),
            "-lcudart_static", "-ldl", "-lpthread", "-lrt", f"-Wl,-rpath,{PKG}"]
     subprocess.run(cmd, check=True, capture_output=True, text=True)
     return exe
+
+
+def _compile(out_dir: str) -> str:
+    return _compile_src(out_dir, "rokoko_infer_main")
 
 
 def test_compat_library_exports_the_reference_seam():

@@ -3,7 +3,7 @@
 -> PCM) on B200, BASELINE config 4, with the config-1 decoder as a nested record.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--batch 32] [--contexts 2] [--workload box|decoder]
+                    [--batch 32] [--contexts 3] [--workload box|decoder|g2p]
 
 Workload: 1024 utterances, token counts from a seeded
 truncated normal (mean 120, sd 60, clipped to [16, 510]) + BOS/EOS, durations
@@ -79,7 +79,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=32)
     p.add_argument("--contexts", type=int, default=3)
-    p.add_argument("--workload", choices=["box", "decoder"], default="box")
+    p.add_argument("--workload", choices=["box", "decoder", "g2p"], default="box")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -659,6 +659,21 @@ def run_decoder_only(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_g2p_only(args, world, rank, local):
+    """--workload g2p: the phonemizer record alone as the JSON line (rank 0)."""
+    import torch
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    rec = g2p_record(dev, args.steps, max(3, args.warmup), cpu_sample=0 if args.no_cpu_baseline else 8)
+    line = {"metric": "phonemizer input characters/sec", "value": rec["value"], "unit": rec["unit"], "n_gpus": 1,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": rec["ms_per_call"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": rec["workload"]}, "e2e": rec["e2e"], "g2p": rec}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_env()
@@ -666,6 +681,8 @@ def main():
         run_reference(args, world, rank)
     elif args.workload == "decoder":
         run_decoder_only(args, world, rank, local)
+    elif args.workload == "g2p":
+        run_g2p_only(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 

@@ -86,6 +86,35 @@ struct Tiles {
     }
 };
 
+// The epilogue's FP32 reads of a tile (residual and accumulator-input rows,
+// whole rows when the channel pitch equals C_out, so that the range is
+// contiguous) are prefetched into L2 when the tile's loads are issued: the
+// reads then hit L2 during the epilogue instead of all CTAs' epilogues pulling
+// them from HBM at once after their MMAs.  Plain row layout only (o_stride 1, no
+// row shift); every prefetched byte lies inside the rows [o_min, T_out).
+__device__ __forceinline__ void prefetch_rows(const float* base, int ld, int r0, int r1) {
+    if (!base || r1 <= r0) return;
+    const char* p = reinterpret_cast<const char*>(base + (size_t)r0 * ld);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t a16 = (a + 15) & ~uintptr_t(15);
+    const uintptr_t end = (a + (size_t)(r1 - r0) * ld * 4) & ~uintptr_t(15);
+    for (uintptr_t q = a16; q < end; q += 32768) {
+        const uintptr_t n = end - q < 32768 ? end - q : 32768;
+        l2_prefetch_bulk(reinterpret_cast<const void*>(q), (uint32_t)n);
+    }
+}
+
+__device__ __forceinline__ void prefetch_epilogue_rows(const ConvArgs& a, int t_tile, int phase, int BN) {
+    if (a.o_stride != 1 || a.res_shift != 0 || a.part_out) return;
+    const int m0 = t_tile * BN;
+    const int rows = min(BN, a.M - m0);
+    int r0 = m0 + a.o_off + phase * a.o_phase_step, r1 = r0 + rows;
+    r0 = max(r0, a.o_min);
+    r1 = min(r1, a.T_out);
+    if (a.res && a.ldres == a.C_out) prefetch_rows(a.res, a.ldres, r0, r1);
+    if (a.acc_in && a.ldacc == a.C_out) prefetch_rows(a.acc_in, a.ldacc, r0, r1);
+}
+
 template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(320, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmX_hi, const __grid_constant__ CUtensorMap tmX_lo,
@@ -144,6 +173,7 @@ __global__ void __launch_bounds__(320, 1)
                 g.decode(t, t_tile, c_tile, phase, ks);
                 const int wrow = phase * args.b_phase_rows + c_tile * CONV_W_ROWS;
                 const int xrow = t_tile * BN + args.a_off + args.min_off;
+                if (ks == S - 1) prefetch_epilogue_rows(args, t_tile, phase, BN);
                 const int kb1 = (ks + 1) * KB / S;
                 for (int kb = ks * KB / S; kb < kb1 && alive; kb++, xi++) {
                     const uint32_t sx = xi % X_STAGES, rx = xi / X_STAGES;

@@ -220,6 +220,9 @@ std::vector<float> copy_f32(const float* p, size_t n) {
 rk_status load_g2p(rk_ctx* c, const uint8_t* blob, size_t n) {
     // src/g2p.h:442-640: magic, header, vocabularies, FP32 weights in file order
     if (n < 48 || std::memcmp(blob, "G2P3", 4) != 0) return fail(RK_ERR_WEIGHTS, "G2P: expected G2P3 format");
+    // the kernels' shared-memory opt-ins (a context may hold a G2P model and no TTS weights)
+    if (conv_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "conv kernel attributes");
+    if (attention_tc_init() != cudaSuccess) return fail_cuda(RK_ERR_CUDA, "attention kernel attributes");
     Reader r{blob, n, 4};
     uint32_t hdr[10];
     for (auto& v : hdr) r.u32(v);

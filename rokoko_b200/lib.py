@@ -16,6 +16,7 @@ RK_OK = 0
 RK_PRECISION_FP32 = 0
 RK_PRECISION_FP16 = 1
 RK_ERR_WORKSPACE = -2
+RK_ERR_DEVICE_TIMEOUT = -7
 RK_CONV_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 _f32p = ctypes.POINTER(ctypes.c_float)

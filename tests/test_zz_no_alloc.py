@@ -80,3 +80,20 @@ def test_static_scratch_rejects_oversize(rk_lib):
     assert b"RK_CONV_STATIC_SCRATCH_BYTES" in rk_lib.rk_last_error()
     torch.cuda.synchronize()
     assert bool((y == 7.0).all())
+
+
+def test_error_word_is_reported_and_cleared(rk_lib):
+    """The conv error word (the first 4 bytes of a workspace, and of the static
+    scratch array that rk_conv1d_static_check reads the same way): a code that a
+    bounded device wait left there is reported once as RK_ERR_DEVICE_TIMEOUT and
+    cleared.  The code is planted by the test (no wait is made to run out)."""
+    from rokoko_b200 import lib
+    dev = torch.device("cuda:0")
+    st = torch.cuda.current_stream().cuda_stream
+    ws = torch.zeros(256, dtype=torch.int32, device=dev)
+    ws[0] = 2  # RK_DEV_TIMEOUT_EMPTY
+    torch.cuda.synchronize()
+    assert rk_lib.rk_conv1d_check(ws.data_ptr(), st) == lib.RK_ERR_DEVICE_TIMEOUT
+    assert int(ws[0].item()) == 0
+    assert rk_lib.rk_conv1d_check(ws.data_ptr(), st) == lib.RK_OK
+    assert rk_lib.rk_conv1d_static_check(st) == lib.RK_OK

@@ -54,11 +54,12 @@ def run_share(ctxs, utts, indices, batch: int, timings=None):
     return run_batches(ctxs, utts, batches, timings)
 
 
-def run_batches(ctxs, utts, batches, timings=None):
+def run_batches(ctxs, utts, batches, timings=None, nvtx: str | None = None):
     """run_share over explicit batches (lists of indices into `utts`): every
     context's host thread takes the next batch not yet taken, so a context that
     drew short utterances takes more batches (the outputs do not depend on
-    which context runs a batch)."""
+    which context runs a batch).  nvtx: name of an NVTX range each host thread
+    holds while it runs batches (NVTX ranges are per thread)."""
     import threading
     results = [[] for _ in ctxs]
     tim = [[0.0, 0.0] for _ in ctxs]
@@ -75,6 +76,9 @@ def run_batches(ctxs, utts, batches, timings=None):
             return b
 
     def worker(c: int) -> None:
+        if nvtx:
+            import torch
+            torch.cuda.nvtx.range_push(nvtx)
         try:
             while True:
                 idx = take()
@@ -90,6 +94,9 @@ def run_batches(ctxs, utts, batches, timings=None):
         except BaseException as e:  # re-raised after the join
             with lock:
                 errors.append(e)
+        finally:
+            if nvtx:
+                torch.cuda.nvtx.range_pop()
 
     threads = [threading.Thread(target=worker, args=(c,)) for c in range(len(ctxs))]
     for th in threads:

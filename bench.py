@@ -3,7 +3,7 @@
 -> PCM) on B200, BASELINE config 4, with the config-1 decoder as a nested record.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--batch 32] [--contexts 3] [--workload box|decoder|g2p]
+                    [--batch 64] [--contexts 3] [--workload box|decoder|g2p]
 
 Workload: 1024 utterances, token counts from a seeded
 truncated normal (mean 120, sd 60, clipped to [16, 510]) + BOS/EOS, durations
@@ -77,7 +77,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--batch", type=int, default=64)
     p.add_argument("--contexts", type=int, default=3)
     p.add_argument("--workload", choices=["box", "decoder", "g2p"], default="box")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -422,6 +422,31 @@ def conv_shapes(timeline, peak_tflops, hbm_gbs, planes=2):
     return out
 
 
+def pack_shapes(timeline, hbm_gbs):
+    """One row per operand-pack shape of a serial profiled decode (the AdaIN /
+    Snake / LeakyReLU + 16-bit operand kernels): launches, us per launch and GB/s
+    for the FP32 source read once and the operand planes written once."""
+    rows = {}
+    prev = 0.0
+    for _sid, name, t in timeline:
+        dt, prev = t - prev, t
+        tok = name.split()
+        if not tok or not tok[0].startswith("pack") or len(tok) < 5 or not tok[1].startswith("C"):
+            continue
+        c, r, cp, rd = int(tok[1][1:]), int(tok[2][1:]), int(tok[3][2:]), int(tok[4][2:])
+        planes = 2 if "split" in tok else 1
+        by = r * c * 4 + rd * cp * 2 * planes
+        key = f"{tok[0]} C{c} R{r}" + (" split" if planes == 2 else "")
+        e = rows.setdefault(key, [0, 0.0, 0.0])
+        e[0] += 1; e[1] += dt; e[2] += by
+    out = []
+    for key, (n, ms, by) in sorted(rows.items(), key=lambda kv: -kv[1][1])[:12]:
+        gbs = by / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+        out.append({"shape": key, "launches": n, "us_per_launch": round(1e3 * ms / n, 2), "gb_s": round(gbs, 1),
+                    "frac_of_hbm": round(gbs / hbm_gbs, 3)})
+    return out
+
+
 def roofline_from(dec, peaks, src):
     conv_ms, conv_flops, conv_n, serial_ms, step_ms = dec.pop("_conv")
     timeline = dec.pop("_timeline", None)
@@ -447,6 +472,7 @@ def roofline_from(dec, peaks, src):
         "step_ms": round(step_ms, 4),
         "workload": "config-1 decoder (L = 400, FP32 semantics) on rank 0",
         "conv_shapes": conv_shapes(timeline, peak, float(peaks.get("hbm_gbs"))) if timeline else None,
+        "pack_shapes": pack_shapes(timeline, float(peaks.get("hbm_gbs"))) if timeline else None,
     }
 
 

@@ -305,7 +305,7 @@ namespace {
 // Decoder + generator for pending utterances [first, first + n): the decoder
 // blocks of up to kDecodeBatch of them per pass (decode_batch.cu), then each
 // one's generator graph; PCM (600 L samples each) to pcm[i] (host, may be null).
-constexpr int kDecodeBatch = 32;
+constexpr int kDecodeBatch = 64;
 
 rk_status decode_entries(rk_ctx* c, size_t first, int n, float* const* pcm) {
     for (int b0 = 0; b0 < n; b0 += kDecodeBatch) {

@@ -150,7 +150,13 @@ void pack(Run& r, const float* x, int ldx, int rows, int C, const Operand& op, i
     }
     cudaError_t e = pack_act(a, split, r.st);
     r.c->launches++;
-    tl_mark(r.c, r.st, coef ? (snake ? "pack_adain_snake" : "pack_adain_lrelu") : "pack");
+    if (r.c->profile && (r.c->prof_mode & RK_PROFILE_TIMELINE)) {
+        // "<kind> C R Cp Rd [split]": source channels and rows, operand columns and rows
+        char nm[96];
+        snprintf(nm, sizeof nm, "%s C%d R%d Cp%d Rd%d%s", coef ? (snake ? "pack_adain_snake" : "pack_adain_lrelu") : "pack",
+                 C, rows, Cp, a.rows_dst, split ? " split" : "");
+        tl_mark(r.c, r.st, nm);
+    }
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "pack_act", e);
 }
 

@@ -123,8 +123,9 @@ void conv(Run& r, const ConvCall& cc) {
         // conv's FLOPs and bytes (res: a residual tensor is read)
         char nm[96];
         int n = snprintf(nm, sizeof nm, "conv %d>%d K%d d%d T%d", w.C_in, w.C_out, w.K, cc.dil, cc.T_out);
-        if (w.phases > 1) n += snprintf(nm + n, sizeof nm - n, " convT %d", cc.rows_in);
-        if (cc.res) snprintf(nm + n, sizeof nm - n, " res");
+        auto room = [&]() { n = n < 0 ? 0 : std::min(n, (int)sizeof nm - 1); return sizeof nm - (size_t)n; };
+        if (w.phases > 1) { const size_t left = room(); n += snprintf(nm + n, left, " convT %d", cc.rows_in); }
+        if (cc.res) { const size_t left = room(); snprintf(nm + n, left, " res"); }
         tl_mark(c, r.st, nm);
     }
     if (e != cudaSuccess) r.status = fail_cuda_err(RK_ERR_LAUNCH, "conv_tc", e);

@@ -44,7 +44,10 @@ constexpr int KC = 64;    // keys per chunk (the S MMA N, the O MMA K)
 constexpr int HD = 64;    // head dim
 constexpr uint32_t ROWB = 128;  // bytes per 64-element 16-bit row
 
-template <bool SPLIT>
+// NBUF buffers of the K, E and V tiles: 2 lets the next chunk's conversion run
+// beside the current chunk's MMA; 1 halves their shared memory (split-bf16:
+// 96 KB instead of 160 KB), so that two CTAs share an SM.
+template <bool SPLIT, int NBUF>
 struct AttCfg {
     static constexpr int NPL = SPLIT ? 2 : 1;
     static constexpr uint32_t Q_PLANE = QT * ROWB;    // 16 KB
@@ -52,10 +55,10 @@ struct AttCfg {
     static constexpr uint32_t E_PLANE = QT * ROWB;    // 16 KB
     static constexpr uint32_t V_PLANE = HD * ROWB;    // 8 KB
     static constexpr uint32_t Q_OFF = 0;
-    static constexpr uint32_t K_OFF = Q_OFF + NPL * Q_PLANE;          // 2 buffers
-    static constexpr uint32_t E_OFF = K_OFF + 2 * NPL * K_PLANE;      // 2 buffers
-    static constexpr uint32_t V_OFF = E_OFF + 2 * NPL * E_PLANE;      // 2 buffers
-    static constexpr uint32_t BYTES = V_OFF + 2 * NPL * V_PLANE;
+    static constexpr uint32_t K_OFF = Q_OFF + NPL * Q_PLANE;
+    static constexpr uint32_t E_OFF = K_OFF + NBUF * NPL * K_PLANE;
+    static constexpr uint32_t V_OFF = E_OFF + NBUF * NPL * E_PLANE;
+    static constexpr uint32_t BYTES = V_OFF + NBUF * NPL * V_PLANE;
 };
 
 // byte offset of 16-bit element (r, k) of a [rows][64] tile in the 128-byte swizzle
@@ -105,10 +108,10 @@ __device__ __forceinline__ void mma_block(uint32_t d_tmem, uint32_t a_hi, uint32
 constexpr int BLOCK_CHUNKS = 7;      // key chunks per block beyond 512 keys
 constexpr uint32_t O_COL_BLOCKED = 448;  // O's TMEM columns when the keys run in blocks
 
-template <bool SPLIT>
+template <bool SPLIT, int NBUF>
 __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restrict__ qkv_all, SegMeta s,
                                                            float* __restrict__ ctx_all, int hid, uint32_t* err) {
-    using C = AttCfg<SPLIT>;
+    using C = AttCfg<SPLIT, NBUF>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t s_bar[2], pv_bar[2], fin_bar;
@@ -173,8 +176,8 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
         const int c1 = min(nch, c0 + bch);
         // ---- phase S: scores of the block's key chunks into TMEM columns [64 (c - c0), +64)
         for (int c = c0; c < c1; c++, gs++) {
-            const int buf = gs & 1;
-            if (gs >= 2 && !mbar_wait(&s_bar[buf], ((gs - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+            const int buf = gs % NBUF;  // the S MMA that last read this K buffer must be done
+            if (gs >= NBUF && !mbar_wait(&s_bar[buf], ((gs - NBUF) / NBUF) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
             if (!__syncthreads_and(ok)) break;
             uint8_t* kh = smem + C::K_OFF + buf * C::NPL * C::K_PLANE;
             uint8_t* kl = kh + C::K_PLANE;
@@ -243,8 +246,8 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
         mx = bmx;
         // ---- pass B: e = exp(s / 8 - max) chunk by chunk, O += E_c V_c
         for (int c = c0; c < c1; c++, gp++) {
-            const int buf = gp & 1;
-            if (gp >= 2 && !mbar_wait(&pv_bar[buf], ((gp - 2) >> 1) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
+            const int buf = gp % NBUF;  // the E V MMA that last read these buffers must be done
+            if (gp >= NBUF && !mbar_wait(&pv_bar[buf], ((gp - NBUF) / NBUF) & 1, err, RK_DEV_TIMEOUT_FULL)) ok = false;
             if (!__syncthreads_and(ok)) break;
             uint8_t* eh = smem + C::E_OFF + buf * C::NPL * C::E_PLANE;
             uint8_t* el = eh + C::E_PLANE;
@@ -323,19 +326,30 @@ __global__ void __launch_bounds__(128) attention_tc_kernel(const float* __restri
     }
 }
 
-constexpr size_t att_smem(bool split) {
-    return (split ? AttCfg<true>::BYTES : AttCfg<false>::BYTES) + 1024;
+template <bool SPLIT, int NBUF>
+constexpr size_t att_smem() {
+    return AttCfg<SPLIT, NBUF>::BYTES + 1024;
+}
+
+template <bool SPLIT, int NBUF>
+cudaError_t att_attr() {
+    return cudaFuncSetAttribute(attention_tc_kernel<SPLIT, NBUF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)att_smem<SPLIT, NBUF>());
+}
+
+template <bool SPLIT, int NBUF>
+void att_launch(dim3 grid, const float* qkv, SegMeta s, float* ctx, int hid, uint32_t* err, cudaStream_t st) {
+    attention_tc_kernel<SPLIT, NBUF><<<grid, 128, att_smem<SPLIT, NBUF>(), st>>>(qkv, s, ctx, hid, err);
 }
 
 }  // namespace
 
 cudaError_t attention_tc_init() {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)att_smem(true));
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)att_smem(false));
-    return e;
+    cudaError_t e;
+    if ((e = att_attr<true, 1>()) || (e = att_attr<true, 2>()) || (e = att_attr<false, 1>()) ||
+        (e = att_attr<false, 2>()))
+        return e;
+    return cudaSuccess;
 }
 
 cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, uint32_t* err, cudaStream_t st,
@@ -343,8 +357,14 @@ cudaError_t attention_tc(const float* qkv, SegMeta s, float* ctx, bool split, ui
     if (heads < 1 || s.n < 1 || s.max_len < 1) return heads < 1 ? cudaErrorInvalidValue : cudaSuccess;
     const dim3 grid((s.max_len + QT - 1) / QT, heads, s.n);
     const int hid = heads * HD;
-    if (split) attention_tc_kernel<true><<<grid, 128, att_smem(true), st>>>(qkv, s, ctx, hid, err);
-    else attention_tc_kernel<false><<<grid, 128, att_smem(false), st>>>(qkv, s, ctx, hid, err);
+    // up to 512 keys (every key's scores in TMEM at once): single K / E / V buffers, two CTAs per
+    // SM; longer sequences (key blocks with online rescaling) keep two buffers.  The arithmetic
+    // is the same either way.
+    const bool single = s.max_len <= 512;
+    if (split) single ? att_launch<true, 1>(grid, qkv, s, ctx, hid, err, st)
+                      : att_launch<true, 2>(grid, qkv, s, ctx, hid, err, st);
+    else single ? att_launch<false, 1>(grid, qkv, s, ctx, hid, err, st)
+                : att_launch<false, 2>(grid, qkv, s, ctx, hid, err, st);
     return cudaGetLastError();
 }
 

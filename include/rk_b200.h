@@ -209,6 +209,17 @@ RK_API rk_status rk_g2p_frames(rk_ctx* ctx, int32_t* ids, size_t cap, size_t* n)
 RK_API size_t rk_g2p_param_bytes(rk_ctx* ctx);
 RK_API void rk_g2p_free(rk_ctx* ctx);
 
+/* IPA -> model input (rokoko::to_tokens / chunk_ipa, src/rokoko.h:141-221),
+ * host only.  rk_ipa_to_tokens: BOS 0, the token id of every code point of
+ * the IPA text that is in the model's vocabulary (others dropped), EOS 0;
+ * *count = ids written (or needed: RK_ERR_WORKSPACE when cap is short; ids
+ * may be NULL to ask).  rk_ipa_chunks: the text split into pieces of at most
+ * 510 code points, after the last . ! ? within the limit, else the last , : ;,
+ * else the last space, else at the limit; ends[k] = end byte offset of piece
+ * k, *n = piece count (ends may be NULL to ask). */
+RK_API rk_status rk_ipa_to_tokens(const char* ipa, size_t bytes, int32_t* ids, size_t cap, size_t* count);
+RK_API rk_status rk_ipa_chunks(const char* ipa, size_t bytes, size_t* ends, size_t cap, size_t* n);
+
 /* Stage activations of the last forward (names as the oracle's stage dumps);
  * copies min(count, cap) floats; *count = element count (0 if unknown). */
 RK_API rk_status rk_get_stage(rk_ctx* ctx, const char* name, float* host_dst, size_t cap, size_t* count);

@@ -81,7 +81,7 @@ def build_compat(force: bool = False) -> str:
     compiled with the system g++."""
     src = os.path.join(HERE, "cpp", "rokoko_compat.cpp")
     hdrs = [os.path.join(INCLUDE, "rokoko", "weights.h"), os.path.join(INCLUDE, "rokoko", "g2p.h"),
-            os.path.join(INCLUDE, "rk_b200.h")]
+            os.path.join(INCLUDE, "rokoko", "tokens.h"), os.path.join(INCLUDE, "rk_b200.h")]
     if not force and not _stale(COMPAT, [src, LIB] + hdrs):
         return COMPAT
     cuda = os.path.dirname(os.path.dirname(NVCC))

@@ -3,9 +3,11 @@
 // rk_create + rk_load_weights_koko, rokoko_infer -> rk_infer (predicted
 // durations, L bucketed by 32 as src/rokoko_f16.cpp:797-802 does); and the
 // reference's phonemizer class (include/rokoko/g2p.h): G2PModelCuda::load ->
-// rk_create + rk_g2p_load, infer -> rk_g2p_infer.
+// rk_create + rk_g2p_load, infer -> rk_g2p_infer; and its IPA helpers
+// (include/rokoko/tokens.h) on rk_ipa_to_tokens / rk_ipa_chunks.
 #include "weights.h"
 #include "g2p.h"
+#include "tokens.h"
 
 #include <cstdio>
 #include <cstring>
@@ -207,4 +209,36 @@ void G2PModelCuda::free() {
 
 size_t G2PModelCuda::param_bytes() const { return ctx_ ? rk_g2p_param_bytes(ctx_) : 0; }
 
+// ------------------------------------------------------------------ IPA -> tokens
+
+std::vector<int32_t> to_tokens(const std::string& phonemes) {
+    size_t n = 0;
+    rk_status s = rk_ipa_to_tokens(phonemes.data(), phonemes.size(), nullptr, 0, &n);
+    if (s != RK_OK) raise("to_tokens", s);
+    std::vector<int32_t> ids(n);
+    s = rk_ipa_to_tokens(phonemes.data(), phonemes.size(), ids.data(), ids.size(), &n);
+    if (s != RK_OK) raise("to_tokens", s);
+    return ids;
+}
+
+std::vector<Chunk> chunk_ipa(const std::string& ipa) {
+    size_t n = 0;
+    rk_status s = rk_ipa_chunks(ipa.data(), ipa.size(), nullptr, 0, &n);
+    if (s != RK_OK) raise("chunk_ipa", s);
+    std::vector<size_t> ends(n);
+    s = rk_ipa_chunks(ipa.data(), ipa.size(), ends.data(), ends.size(), &n);
+    if (s != RK_OK) raise("chunk_ipa", s);
+    std::vector<Chunk> out;
+    size_t start = 0;
+    for (size_t e : ends) {
+        Chunk c;
+        c.phonemes = ipa.substr(start, e - start);
+        c.tokens = to_tokens(c.phonemes);
+        out.push_back(std::move(c));
+        start = e;
+    }
+    return out;
+}
+
 }  // namespace rokoko
+

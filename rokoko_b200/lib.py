@@ -86,6 +86,11 @@ SIGNATURES = [
      [ctypes.c_void_p, _i32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
     ("rk_g2p_param_bytes", ctypes.c_size_t, [ctypes.c_void_p]),
     ("rk_g2p_free", None, [ctypes.c_void_p]),
+    ("rk_ipa_to_tokens", ctypes.c_int,
+     [ctypes.c_char_p, ctypes.c_size_t, _i32p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    ("rk_ipa_chunks", ctypes.c_int,
+     [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.c_size_t,
+      ctypes.POINTER(ctypes.c_size_t)]),
     ("rk_profile", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     ("rk_profile_read", ctypes.c_int,
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),

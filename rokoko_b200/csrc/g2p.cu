@@ -544,7 +544,7 @@ extern "C" rk_status rk_g2p_infer(rk_ctx* c, const char* const* texts, const siz
     std::vector<std::vector<int32_t>> ids(n);
     std::vector<uint32_t> cps;
     std::vector<int> row_off(n, -1), len(n, 0);
-    int R = 0, nb = 0, max_len = 0;
+    int R = 0;
     for (int i = 0; i < n; i++) {
         utf8_codepoints(texts[i], text_bytes[i], cps);
         if (cps.empty() || (int)cps.size() > G2P_MAX_POS) continue;
@@ -556,44 +556,57 @@ extern "C" rk_status rk_g2p_infer(rk_ctx* c, const char* const* texts, const siz
         row_off[i] = R;
         len[i] = (int)cps.size();
         R += len[i];
-        max_len = std::max(max_len, len[i]);
-        nb++;
     }
-    s.ws.last_best.clear();
-    if (R > 0) {
-        rk_status st = ensure_g2p_ws(c, R, nb);
-        if (st) return st;
-        G2PWS& w = s.ws;
-        int32_t* h = static_cast<int32_t*>(w.h_stage);
-        int k = 0;
-        for (int i = 0; i < n; i++) {
-            if (row_off[i] < 0) continue;
-            for (int t = 0; t < len[i]; t++) { h[row_off[i] + t] = ids[i][t]; h[R + row_off[i] + t] = t; }
-            h[2 * R + k] = row_off[i];
-            h[2 * R + nb + k] = len[i];
-            k++;
+    // device passes over groups of consecutive texts (bounded workspace and grid: a launch's
+    // grid holds at most 65535 texts); per-text results do not depend on the grouping
+    constexpr int kGroupTexts = 4096, kGroupRows = 1 << 18;
+    s.ws.last_best.assign((size_t)R * m.up, 0);
+    for (int i0 = 0; i0 < n;) {
+        int i1 = i0, rows_g = 0, texts_g = 0, max_g = 0;
+        while (i1 < n && (row_off[i1] < 0 || texts_g == 0 ||
+                          (texts_g < kGroupTexts && rows_g + len[i1] <= kGroupRows))) {
+            if (row_off[i1] >= 0) { rows_g += len[i1]; texts_g++; max_g = std::max(max_g, len[i1]); }
+            i1++;
         }
-        if (cudaMemcpyAsync(w.meta, h, (2 * (size_t)R + 2 * (size_t)nb) * 4, cudaMemcpyHostToDevice, c->stream) !=
-            cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, "G2P metadata upload");
-        Run r{c, c->stream, true};
-        enqueue_g2p(r, s, R, nb, max_len);
-        if (r.status) {
-            cudaStreamSynchronize(c->stream);
-            return r.status;
+        if (texts_g > 0) {
+            int base = -1;
+            for (int i = i0; i < i1 && base < 0; i++) base = row_off[i];
+            rk_status st = ensure_g2p_ws(c, rows_g, texts_g);
+            if (st) return st;
+            G2PWS& w = s.ws;
+            int32_t* h = static_cast<int32_t*>(w.h_stage);
+            int k = 0;
+            for (int i = i0; i < i1; i++) {
+                if (row_off[i] < 0) continue;
+                const int o = row_off[i] - base;
+                for (int t = 0; t < len[i]; t++) { h[o + t] = ids[i][t]; h[rows_g + o + t] = t; }
+                h[2 * rows_g + k] = o;
+                h[2 * rows_g + texts_g + k] = len[i];
+                k++;
+            }
+            if (cudaMemcpyAsync(w.meta, h, (2 * (size_t)rows_g + 2 * (size_t)texts_g) * 4, cudaMemcpyHostToDevice,
+                                c->stream) != cudaSuccess)
+                return fail_cuda(RK_ERR_CUDA, "G2P metadata upload");
+            Run r{c, c->stream, true};
+            enqueue_g2p(r, s, rows_g, texts_g, max_g);
+            if (r.status) {
+                cudaStreamSynchronize(c->stream);
+                return r.status;
+            }
+            const size_t frames = (size_t)rows_g * m.up;
+            if (cudaMemcpyAsync(h, w.best, frames * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+                return fail_cuda(RK_ERR_CUDA, "G2P frame read-back");
+            uint32_t e = 0;
+            cudaError_t ce = cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->stream);
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
+            if (ce != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "G2P device sync", ce);
+            if (e) {
+                cudaMemsetAsync(c->err, 0, 4, c->stream);
+                return fail(RK_ERR_DEVICE_TIMEOUT, "G2P: a device-side wait gave up");
+            }
+            std::memcpy(s.ws.last_best.data() + (size_t)base * m.up, h, frames * 4);
         }
-        const size_t rows = (size_t)R * m.up;
-        if (cudaMemcpyAsync(h, w.best, rows * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-            return fail_cuda(RK_ERR_CUDA, "G2P frame read-back");
-        uint32_t e = 0;
-        cudaError_t ce = cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->stream);
-        if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->stream);
-        if (ce != cudaSuccess) return fail_cuda_err(RK_ERR_CUDA, "G2P device sync", ce);
-        if (e) {
-            cudaMemsetAsync(c->err, 0, 4, c->stream);
-            return fail(RK_ERR_DEVICE_TIMEOUT, "G2P: a device-side wait gave up");
-        }
-        w.last_best.assign(h, h + rows);
+        i0 = i1;
     }
     // CTC per text (src/g2p.h:865-882): drop blank 0 and repeats, id -> phone -> UTF-8
     size_t used = 0;

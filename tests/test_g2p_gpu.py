@@ -165,3 +165,20 @@ def test_cpp_g2p_caller(blob, model):
         with open(op, encoding="utf-8") as f:
             got = f.read().split("\n")[:-1]
     assert got == model.infer_batch(texts)
+
+
+def test_calls_beyond_one_device_pass(model):
+    """More than 4096 texts, or more than 2^18 characters, run as several device
+    passes; every text's ids are those of the same text in a smaller call."""
+    short = [g2pfile.random_texts(1, seed=100 + (i % 7), mean=5, sd=2, lo=1, hi=9)[0] for i in range(4100)]
+    out = model.infer_batch(short)
+    f = model.frames()
+    a, fa = model.infer_batch(short[:4096]), model.frames()
+    b, fb = model.infer_batch(short[4096:]), model.frames()
+    assert out == a + b and np.array_equal(f, np.concatenate([fa, fb]))
+    long = [g2pfile.random_texts(1, seed=200 + i, mean=2048, sd=0, lo=2048, hi=2048)[0] for i in range(130)]
+    out = model.infer_batch(long)
+    f = model.frames()
+    a, fa = model.infer_batch(long[:64]), model.frames()
+    b, fb = model.infer_batch(long[64:]), model.frames()
+    assert out == a + b and np.array_equal(f, np.concatenate([fa, fb]))

@@ -54,26 +54,56 @@ def run_share(ctxs, utts, indices, batch: int, timings=None):
     return run_batches(ctxs, utts, batches, timings)
 
 
-def run_batches(ctxs, utts, batches, timings=None, nvtx: str | None = None):
+def run_batches(ctxs, utts, batches, timings=None, nvtx: str | None = None, failures: list | None = None,
+                max_tries: int = 2):
     """run_share over explicit batches (lists of indices into `utts`): every
     context's host thread takes the next batch not yet taken, so a context that
     drew short utterances takes more batches (the outputs do not depend on
     which context runs a batch).  nvtx: name of an NVTX range each host thread
-    holds while it runs batches (NVTX ranges are per thread)."""
+    holds while it runs batches (NVTX ranges are per thread).
+
+    Failure handling: a context whose encode or decode raises is taken out of
+    service (its thread stops) and the batch goes back to the front of the
+    queue for another context, up to `max_tries` attempts per batch; `failures`
+    (if given) receives (context, batch, error text) for each failed attempt.
+    The call raises when a batch has failed `max_tries` times or when no
+    context is left in service."""
     import threading
     results = [[] for _ in ctxs]
     tim = [[0.0, 0.0] for _ in ctxs]
-    errors = []
-    lock = threading.Lock()
-    nxt = [0]
+    fatal = []
+    cond = threading.Condition()
+    queue = list(range(len(batches)))[::-1]  # pop() from the end = next batch
+    tries = [0] * len(batches)
+    alive = [True] * len(ctxs)
+    inflight = [0]
 
     def take():
-        with lock:
-            if errors or nxt[0] >= len(batches):
-                return None
-            b = batches[nxt[0]]
-            nxt[0] += 1
-            return b
+        # the next batch; with the queue empty, wait while batches are in flight (one may come back)
+        with cond:
+            while True:
+                if fatal:
+                    return None
+                if queue:
+                    inflight[0] += 1
+                    return queue.pop()
+                if inflight[0] == 0:
+                    return None
+                cond.wait()
+
+    def finished(c: int, bi: int, err) -> None:
+        with cond:
+            inflight[0] -= 1
+            if err is not None:
+                alive[c] = False
+                tries[bi] += 1
+                if failures is not None:
+                    failures.append((c, bi, repr(err)))
+                if tries[bi] >= max_tries or not any(alive):
+                    fatal.append(err)
+                else:
+                    queue.append(bi)
+            cond.notify_all()
 
     def worker(c: int) -> None:
         if nvtx:
@@ -81,19 +111,22 @@ def run_batches(ctxs, utts, batches, timings=None, nvtx: str | None = None):
             torch.cuda.nvtx.range_push(nvtx)
         try:
             while True:
-                idx = take()
-                if idx is None:
+                bi = take()
+                if bi is None:
                     return
-                te = time.perf_counter()
-                _, Ls = ctxs[c].encode([utts[i] for i in idx])
-                td = time.perf_counter()
-                pcms = ctxs[c].decode(Ls)
+                idx = batches[bi]
+                try:
+                    te = time.perf_counter()
+                    _, Ls = ctxs[c].encode([utts[i] for i in idx])
+                    td = time.perf_counter()
+                    pcms = ctxs[c].decode(Ls)
+                except BaseException as e:  # this context leaves service; the batch is retried
+                    finished(c, bi, e)
+                    return
                 tim[c][0] += td - te
                 tim[c][1] += time.perf_counter() - td
                 results[c].extend(zip(idx, pcms))
-        except BaseException as e:  # re-raised after the join
-            with lock:
-                errors.append(e)
+                finished(c, bi, None)
         finally:
             if nvtx:
                 torch.cuda.nvtx.range_pop()
@@ -103,8 +136,10 @@ def run_batches(ctxs, utts, batches, timings=None, nvtx: str | None = None):
         th.start()
     for th in threads:
         th.join()
-    if errors:
-        raise errors[0]
+    if fatal:
+        raise fatal[0]
+    if queue:  # every context left service with batches still queued
+        raise RuntimeError(f"{len(queue)} batches not run: no context left in service")
     if timings is not None:
         timings[:] = tim
     return [x for r in results for x in r]

@@ -369,6 +369,7 @@ def g2p_record(dev, steps: int, warmup: int, n_texts: int = 256, cpu_sample: int
                    "h2d_bytes_per_step": 8 * chars + 8 * n_texts, "d2h_bytes_per_step": 12 * chars}}
     if cpu_sample > 0:
         import oracle
+        oracle.set_threads(host_threads())
         o = oracle.G2POracle(blob)
         sub = texts[:cpu_sample]
         t0 = time.perf_counter()

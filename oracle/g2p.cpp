@@ -22,6 +22,7 @@
 // Products and sums are FP32; the GEMMs use the oracle's blocked kernel
 // (gemm.cpp), whose summation order differs from the reference's TF32
 // tensor-core GEMMs, so logits agree to a tolerance, not bitwise.
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -161,9 +162,12 @@ void forward(const G2P& m, const std::vector<int>& ids, std::vector<float>& logi
                         b[d2 + i] = x1 * c + x0 * s;
                     }
                 }
-        orc::parallel_for(H, [&](int hh) {
+        // work items = (head, block of 64 queries); each query's arithmetic is the same in any split
+        const int qblk = (T + 63) / 64;
+        orc::parallel_for(H * qblk, [&](int item) {
+            const int hh = item / qblk, q0 = (item % qblk) * 64, q1 = std::min(T, q0 + 64);
             std::vector<float> p(T);
-            for (int q = 0; q < T; q++) {
+            for (int q = q0; q < q1; q++) {
                 const float* qv = &qkv[(size_t)q * 3 * d + hh * dk];
                 float mx = -1e30f;
                 for (int k = 0; k < T; k++) {

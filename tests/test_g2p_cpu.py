@@ -39,6 +39,7 @@ def blob():
 
 @pytest.fixture(scope="module")
 def g2p_oracle(blob):
+    oracle.set_threads(max(1, os.cpu_count() or 1))
     o = oracle.G2POracle(blob)
     yield o
     o.close()
